@@ -1,0 +1,8 @@
+// boa_all.cu -- the library's single translation unit.  Kernels, launchers and
+// the host runtime are compiled together so that device globals (the error
+// word read back by the host) have exactly one definition without relocatable
+// device code.
+#include "gemm.cu"
+#include "mamba.cu"
+#include "runtime.cpp"
+#include "container.cpp"

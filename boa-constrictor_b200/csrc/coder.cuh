@@ -1,0 +1,272 @@
+// coder.cuh -- softmax -> integer CDF and the 64-bit/32-bit-word range coder,
+// as device functions shared by the LM-head epilogue (compress and decompress)
+// and the standalone coder kernels.
+//
+// CDF: the reference builds it with one warp per row, lane l owning symbols
+// 8l..8l+7 (range_coder_kernels.cu:860-925, decode twin :661-763).  Here ONE
+// thread evaluates the same arithmetic in the same order (lane partial sums,
+// shfl_down reduction tree, Hillis-Steele scan, lane-boundary monotone fix-up,
+// Q_k = (u32)(C_k * (2^24 - 256)) + k), using explicit round-to-nearest
+// intrinsics so no operation is contracted.  Encoder and decoder therefore see
+// bit-identical Q_k, and for identical exponentials the values equal the
+// reference's.
+//
+// Coder: restates ker_rc_init (:46-60), the encode update (:927-965),
+// ker_rc_finish (:279-313), ker_rc_init_decoder (:319-335) and the decode
+// update (:765-780).  Pure integer arithmetic -> bit-exact.
+#pragma once
+#include <cstdint>
+#include "ptx.cuh"
+
+namespace boa {
+
+constexpr uint32_t kCdfTotal = 1u << 24;
+constexpr double kCdfScale = (double)((1u << 24) - 256);
+
+struct EncState {  // RCState, gemm_gpu.hpp:115-121
+  unsigned long long lower, range;
+  int inv;             // inverted_num: pending carry-run length
+  uint32_t first_inv;  // first_inv_lower_word
+  int w;               // words written
+  int pad;
+};
+struct DecState {  // RCDecState, gemm_gpu.hpp:212-217
+  unsigned long long lower, range, point;
+  int r;  // words consumed
+  int n;  // words available
+};
+
+__host__ __device__ __forceinline__ void enc_init(EncState& s) {
+  s.lower = 0ull; s.range = ~0ull; s.inv = 0; s.first_inv = 0u; s.w = 0; s.pad = 0;
+}
+
+// Encode one symbol with CDF slot [left, left+prob) of 2^24.  Returns false
+// (and stops writing) when the stream would exceed `cap` words.
+__device__ __forceinline__ bool enc_symbol(EncState& st, uint32_t left, uint32_t prob, uint32_t* out,
+                                           int cap) {
+  if (prob == 0) prob = 1;
+  const unsigned long long scale = st.range >> 24;
+  const unsigned long long old_lower = st.lower;
+  st.range = scale * (unsigned long long)prob;
+  st.lower = st.lower + scale * (unsigned long long)left;
+  if (st.inv > 0) {
+    const unsigned long long sum = st.lower + st.range;
+    if (sum > st.lower) {
+      const bool carried = st.lower < old_lower;
+      const uint32_t first = carried ? st.first_inv + 1u : st.first_inv;
+      const uint32_t sub = carried ? 0u : 0xFFFFFFFFu;
+      if (st.w + st.inv > cap) return false;
+      out[st.w++] = first;
+      for (int k = 1; k < st.inv; ++k) out[st.w++] = sub;
+      st.inv = 0;
+    }
+  }
+  while (st.range < (1ull << 32)) {
+    const uint32_t lw = (uint32_t)(st.lower >> 32);
+    st.lower <<= 32;
+    st.range <<= 32;
+    if (st.inv > 0) {
+      st.inv++;
+    } else {
+      const unsigned long long sum = st.lower + st.range;
+      if (sum > st.lower) {
+        if (st.w >= cap) return false;
+        out[st.w++] = lw;
+      } else {
+        st.inv = 1;
+        st.first_inv = lw;
+      }
+    }
+  }
+  return true;
+}
+
+// Flush; returns total words (0 if nothing was encoded) or -1 on overflow.
+__device__ __forceinline__ int enc_finish(EncState& st, uint32_t* out, int cap) {
+  if (st.range == ~0ull) return 0;
+  const unsigned long long point = st.lower + ((1ull << 32) - 1ull);
+  if (st.inv > 0) {
+    const bool carried = point < st.lower;
+    const uint32_t first = carried ? st.first_inv + 1u : st.first_inv;
+    const uint32_t sub = carried ? 0u : 0xFFFFFFFFu;
+    if (st.w + st.inv > cap) return -1;
+    out[st.w++] = first;
+    for (int k = 1; k < st.inv; ++k) out[st.w++] = sub;
+    st.inv = 0;
+  }
+  const uint32_t pw = (uint32_t)(point >> 32);
+  if (st.w + 2 > cap) return -1;
+  out[st.w++] = pw;
+  const unsigned long long upper = st.lower + st.range;
+  if ((uint32_t)(upper >> 32) == pw) out[st.w++] = 0u;
+  return st.w;
+}
+
+__device__ __forceinline__ void dec_init(DecState& st, const uint32_t* in, int n) {
+  st.lower = 0ull; st.range = ~0ull; st.point = 0ull; st.r = 0; st.n = n;
+  for (int k = 0; k < 2; ++k) {
+    const uint32_t w = st.r < n ? in[st.r++] : 0u;
+    st.point = (st.point << 32) | (unsigned long long)w;
+  }
+}
+__device__ __forceinline__ uint32_t dec_target(const DecState& st) {
+  const unsigned long long scale = st.range >> 24;
+  unsigned long long q = (st.point - st.lower) / scale;
+  if (q >= (1ull << 24)) q = (1ull << 24) - 1ull;
+  return (uint32_t)q;
+}
+__device__ __forceinline__ void dec_update(DecState& st, uint32_t low, uint32_t high, const uint32_t* in) {
+  const unsigned long long scale = st.range >> 24;
+  uint32_t prob = high - low;
+  if (prob == 0) prob = 1;
+  st.lower = st.lower + scale * (unsigned long long)low;
+  st.range = scale * (unsigned long long)prob;
+  while (st.range < (1ull << 32)) {
+    st.lower <<= 32;
+    st.range <<= 32;
+    const uint32_t w = st.r < st.n ? in[st.r++] : 0u;
+    st.point = (st.point << 32) | (unsigned long long)w;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// softmax -> CDF for one row held by one thread.
+// Src must provide: __device__ void lane(int l, float (&v)[8]) const
+// returning the 8 logits (bias already added) of symbols 8l..8l+7.
+// ---------------------------------------------------------------------------
+struct CdfRow {
+  float mx;
+  float inv_t;
+  double inv_sum;
+  double ws[32];  // reference "warp_start" of each lane (pre fix-up CDF at 8l)
+};
+
+__device__ __forceinline__ float cdf_exp(float v, float mx, float inv_t) {
+  return __expf(__fmul_rn(__fsub_rn(v, mx), inv_t));
+}
+
+template <class Src>
+__device__ __forceinline__ void cdf_prepare(const Src& src, float inv_t, CdfRow& R) {
+  float mx = -1e30f;
+#pragma unroll 1
+  for (int l = 0; l < 32; ++l) {
+    float v[8];
+    src.lane(l, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mx = fmaxf(mx, v[i]);
+  }
+  R.mx = mx;
+  R.inv_t = inv_t;
+  double ts[32];
+#pragma unroll 1
+  for (int l = 0; l < 32; ++l) {
+    float v[8];
+    src.lane(l, v);
+    double sd = 0.0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sd = __dadd_rn(sd, (double)cdf_exp(v[i], mx, inv_t));
+    ts[l] = sd;
+    R.ws[l] = sd;
+  }
+  // shfl_down reduction tree; only lanes < off feed lane 0's result
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int l = 0; l < off; ++l) R.ws[l] = __dadd_rn(R.ws[l], R.ws[l + off]);
+  const double inv_sum = 1.0 / R.ws[0];
+  R.inv_sum = inv_sum;
+#pragma unroll
+  for (int l = 0; l < 32; ++l) {
+    ts[l] = __dmul_rn(ts[l], inv_sum);
+    R.ws[l] = ts[l];
+  }
+  // inclusive Hillis-Steele scan (shfl_up); descending l reads old values
+#pragma unroll
+  for (int off = 1; off <= 16; off <<= 1)
+#pragma unroll
+    for (int l = 31; l >= off; --l) R.ws[l] = __dadd_rn(R.ws[l], R.ws[l - off]);
+#pragma unroll
+  for (int l = 0; l < 32; ++l) R.ws[l] = __dsub_rn(R.ws[l], ts[l]);
+}
+
+// pre-fix-up running CDF values of lane l: p[j] = cdf[8l+j], and the lane's
+// 8th value p[7] (the "prev_end" its right neighbour compares against).
+template <class Src>
+__device__ __forceinline__ void cdf_lane(const Src& src, const CdfRow& R, int l, double (&p)[8]) {
+  float v[8];
+  src.lane(l, v);
+  double run = R.ws[l];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    p[i] = run;
+    run = __dadd_rn(run, __dmul_rn((double)cdf_exp(v[i], R.mx, R.inv_t), R.inv_sum));
+  }
+}
+__device__ __forceinline__ double cdf_fix(double my_start, double prev_end) {
+  return my_start < prev_end ? __dsub_rn(prev_end, my_start) : 0.0;
+}
+__device__ __forceinline__ double cdf_post(double pre, double delta) {
+  return delta != 0.0 ? __dadd_rn(pre, delta) : pre;
+}
+__device__ __forceinline__ uint32_t cdf_q(double c, int k) {
+  return (uint32_t)__dmul_rn(c, kCdfScale) + (uint32_t)k;
+}
+
+// [low, high) of symbol s (encoder side, range_coder_kernels.cu:917-925)
+template <class Src>
+__device__ __forceinline__ void cdf_symbol(const Src& src, const CdfRow& R, int s, uint32_t& low,
+                                           uint32_t& high) {
+  const int L = s >> 3, i = s & 7;
+  double p[8];
+  double dL = 0.0;
+  if (L > 0) {
+    cdf_lane(src, R, L - 1, p);
+    dL = cdf_fix(R.ws[L], p[7]);
+  }
+  cdf_lane(src, R, L, p);
+  low = cdf_q(cdf_post(p[i], dL), s);
+  if (s == 255) {
+    high = kCdfTotal;
+  } else if (i < 7) {
+    high = cdf_q(cdf_post(p[i + 1], dL), s + 1);
+  } else {
+    const double d1 = cdf_fix(R.ws[L + 1], p[7]);
+    high = cdf_q(cdf_post(R.ws[L + 1], d1), s + 1);
+  }
+}
+
+// Decoder search: lowest s with Q_s <= target < Q_{s+1}
+// (warp ballot + __ffs in range_coder_kernels.cu:747-763 picks the lowest).
+template <class Src>
+__device__ __forceinline__ int cdf_search(const Src& src, const CdfRow& R, uint32_t target, uint32_t& low,
+                                          uint32_t& high) {
+  double dl = 0.0;  // fix-up delta of the current lane
+#pragma unroll 1
+  for (int l = 0; l < 32; ++l) {
+    double p[8];
+    cdf_lane(src, R, l, p);
+    double next0 = 1.0, dn = 0.0;
+    if (l < 31) {
+      dn = cdf_fix(R.ws[l + 1], p[7]);
+      next0 = cdf_post(R.ws[l + 1], dn);
+    }
+    uint32_t q = cdf_q(cdf_post(p[0], dl), 8 * l);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int k = 8 * l + j;
+      const uint32_t qn = (k == 255) ? kCdfTotal : cdf_q(j < 7 ? cdf_post(p[j + 1], dl) : next0, k + 1);
+      if (target >= q && target < qn) {
+        low = q;
+        high = qn;
+        return k;
+      }
+      q = qn;
+    }
+    dl = dn;
+  }
+  low = 0u;
+  high = 0u;
+  return 0;
+}
+
+}  // namespace boa

@@ -1,0 +1,402 @@
+// gemm.cu -- tcgen05 GEMM for sm_100a with fused epilogues.
+//
+// Replaces the reference's SIMT fp32 GEMM (ker_gemm_register_tiled_64x64_strided,
+// gemm_kernels.cu:176-314, launchers :378-426) and the elementwise kernels it
+// was followed by (LayerNorm inference_kernels.cu:229-348, the head's softmax
+// and CDF in range_coder_kernels.cu:860-925 / :661-763).
+//
+// CTA tile 128 x BN, K-blocks of 64.  Warp roles (192 threads):
+//   warp 0      TMA producer: A hi/lo tiles (128x64) + W hi/lo tiles (BNx64)
+//   warp 1      TMEM allocator; lane 0 issues tcgen05.mma (3 per K=16 step:
+//               Ah*Wh, Ah*Wl, Al*Wh -> ~fp32 accuracy from bf16 tensor cores)
+//   warps 2..5  epilogue: one accumulator row per thread (TMEM lane quarter
+//               = warp % 4), fused bias / activation / LayerNorm / residual /
+//               LM-head coder.
+// No split-K, a fixed K order and one instruction shape: a row's result does
+// not depend on M or on where the row sits in the tile, so the compress
+// (M = chunks x tokens) and decompress (M = chunks) paths produce bit-identical
+// logits and therefore identical CDFs.
+#include <cuda.h>
+#include <cstdio>
+#include <mutex>
+#include "gemm.cuh"
+
+namespace boa {
+
+constexpr int kBM = 128, kBK = 64;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStages = BN >= 256 ? 2 : (BN >= 128 ? 3 : 4);
+  static constexpr int kABytes = kBM * kBK * 2;  // one plane, 16 KB
+  static constexpr int kBBytes = BN * kBK * 2;   // one plane
+  static constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;
+  static constexpr int kTmemCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+  if (act == ACT_GELU) {
+    const float k0 = 0.79788456080286535588f, k1 = 0.044715f;
+    return 0.5f * v * (1.0f + tanhf(k0 * (v + k1 * v * v * v)));
+  }
+  if (act == ACT_RELU) return fmaxf(0.0f, v);
+  if (act == ACT_SILU) return v / (1.0f + __expf(-v));
+  return v;
+}
+
+__device__ __forceinline__ void store_split16(__nv_bfloat16* hi, __nv_bfloat16* lo, const float (&v)[16]) {
+  __align__(16) __nv_bfloat16 h[16];
+  __align__(16) __nv_bfloat16 l[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) split_bf16(v[j], h[j], l[j]);
+  reinterpret_cast<uint4*>(hi)[0] = reinterpret_cast<uint4*>(h)[0];
+  reinterpret_cast<uint4*>(hi)[1] = reinterpret_cast<uint4*>(h)[1];
+  reinterpret_cast<uint4*>(lo)[0] = reinterpret_cast<uint4*>(l)[0];
+  reinterpret_cast<uint4*>(lo)[1] = reinterpret_cast<uint4*>(l)[1];
+}
+__device__ __forceinline__ void store_f32x16(float* p, const float (&v)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; j += 4) reinterpret_cast<float4*>(p)[j / 4] = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+}
+
+// row source for the CDF code: one logits row staged in shared memory
+struct SmemRow {
+  const float* p;
+  __device__ __forceinline__ void lane(int l, float (&v)[8]) const {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = p[l * 8 + i];
+  }
+};
+constexpr int kRowStride = 257;  // floats; odd stride -> conflict-free per-thread rows
+
+template <int BN, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, GemmArgs args) {
+  using Cfg = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes);
+  uint64_t* full = bars;                      // [kStages]
+  uint64_t* empty = bars + Cfg::kStages;      // [kStages]
+  uint64_t* acc_full = bars + 2 * Cfg::kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * Cfg::kStages + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN;
+  const int m0 = blockIdx.y * kBM;
+  const int nkb = (args.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmW);
+  }
+  if (warp == 1) { tmem_alloc(tmem_slot, Cfg::kTmemCols); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % Cfg::kStages;
+        if (kb >= Cfg::kStages) {
+          if (!mbar_wait(&empty[s], ((kb / Cfg::kStages) - 1) & 1)) { *abort_flag = 1; break; }
+        }
+        if (*abort_flag) break;
+        uint8_t* st = smem + s * Cfg::kStageBytes;
+        mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+        const int k0 = kb * kBK;
+        tma_load_3d(st, &tmA, &full[s], k0, m0, 0);
+        tma_load_3d(st + Cfg::kABytes, &tmA, &full[s], k0, m0, 1);
+        tma_load_3d(st + 2 * Cfg::kABytes, &tmW, &full[s], k0, n0, 0);
+        tma_load_3d(st + 2 * Cfg::kABytes + Cfg::kBBytes, &tmW, &full[s], k0, n0, 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % Cfg::kStages;
+        if (!mbar_wait(&full[s], (kb / Cfg::kStages) & 1)) { *abort_flag = 1; break; }
+        if (*abort_flag) break;
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + s * Cfg::kStageBytes);
+        const uint64_t dAh = umma_desc_sw128(st);
+        const uint64_t dAl = umma_desc_sw128(st + Cfg::kABytes);
+        const uint64_t dWh = umma_desc_sw128(st + 2 * Cfg::kABytes);
+        const uint64_t dWl = umma_desc_sw128(st + 2 * Cfg::kABytes + Cfg::kBBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          const uint64_t adv = (uint64_t)(kk * 32 >> 4);  // 16 bf16 = 32 B along K
+          umma_bf16(tmem, dAh + adv, dWh + adv, idesc, (kb | kk) != 0);
+          umma_bf16(tmem, dAh + adv, dWl + adv, idesc, 1u);
+          umma_bf16(tmem, dAl + adv, dWh + adv, idesc, 1u);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(acc_full);
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r_local = q * 32 + lane;
+    const int row = m0 + r_local;
+    const bool ok = mbar_wait(acc_full, 0);
+    tc_fence_after();
+    if (ok && !*abort_flag) {
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+      const bool live = row < args.M;
+      if constexpr (MODE == EPI_F32 || MODE == EPI_LOGITS) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          float v[16];
+          tmem_ld16(trow + c, v);
+          if (args.bias) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += args.bias[n0 + c + j];
+          }
+          if (live) store_f32x16(args.out_f32 + (size_t)row * args.ld_f32 + n0 + c, v);
+        }
+      } else if constexpr (MODE == EPI_ACT_SPLIT) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          float v[16];
+          tmem_ld16(trow + c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = apply_act(v[j] + args.bias[n0 + c + j], args.act);
+          if (live) {
+            __nv_bfloat16* hi = args.out_hl + (size_t)row * args.ld_hl + n0 + c;
+            store_split16(hi, hi + args.plane_hl, v);
+          }
+        }
+      } else if constexpr (MODE == EPI_LN_SPLIT || MODE == EPI_RES_LN) {
+        // full row in this tile (BN == N); pass 1: values + moments
+        float sum = 0.f, sq = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          float v[16];
+          tmem_ld16(trow + c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float x = v[j] + args.bias[c + j];
+            if constexpr (MODE == EPI_RES_LN) x = x + (live ? args.res[(size_t)row * BN + c + j] : 0.f);
+            v[j] = x;
+            sum += x;
+            sq += x * x;
+          }
+          if constexpr (MODE == EPI_RES_LN) {
+            if (live) store_f32x16(args.res + (size_t)row * BN + c, v);
+          }
+        }
+        const bool norm = args.ln_w != nullptr;
+        const float mean = sum / (float)BN;
+        const float var = sq / (float)BN - mean * mean;
+        const float inv_std = rsqrtf(var + 1e-5f);
+        // pass 2: normalise (or plain split of x for the head) and store
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          float v[16];
+          if constexpr (MODE == EPI_RES_LN) {
+            if (live) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                float4 t = reinterpret_cast<const float4*>(args.res + (size_t)row * BN + c)[j / 4];
+                v[j] = t.x; v[j + 1] = t.y; v[j + 2] = t.z; v[j + 3] = t.w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = 0.f;
+            }
+          } else {
+            tmem_ld16(trow + c, v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = v[j] + args.bias[c + j];
+          }
+          if (norm) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = (v[j] - mean) * inv_std * args.ln_w[c + j] + args.ln_b[c + j];
+          }
+          if (live) {
+            __nv_bfloat16* hi = args.out_hl + (size_t)row * args.ld_hl + c;
+            store_split16(hi, hi + args.plane_hl, v);
+          }
+        }
+      } else if constexpr (MODE == EPI_HEAD_ENC || MODE == EPI_HEAD_DEC) {
+        // stage the row (logits + bias) in the now idle pipeline smem
+        float* srow = reinterpret_cast<float*>(smem) + (size_t)r_local * kRowStride;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          float v[16];
+          tmem_ld16(trow + c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) srow[c + j] = v[j] + args.bias[c + j];
+        }
+        __syncwarp();
+        if (live) {
+          SmemRow src{srow};
+          if constexpr (MODE == EPI_HEAD_ENC) {
+            const int b = row / args.T, tau = row - b * args.T;
+            const long long base = (long long)b * args.chunk_len;
+            const long long rem = args.n_bytes - base;
+            const int len = (int)(rem < args.chunk_len ? rem : args.chunk_len);
+            const int p = args.t0 + tau;
+            uint2 lh = make_uint2(0u, 0u);
+            if (p + 1 < len) {
+              CdfRow R;
+              cdf_prepare(src, args.inv_t, R);
+              const int s = args.tokens[base + p + 1];
+              cdf_symbol(src, R, s, lh.x, lh.y);
+            }
+            args.lf[row] = lh;
+          } else {
+            const int b = row;
+            const int t = *args.d_t;
+            const long long base = (long long)b * args.chunk_len;
+            const long long rem = args.n_bytes - base;
+            const int len = (int)(rem < args.chunk_len ? rem : args.chunk_len);
+            if (t < len) {
+              DecState st = args.dstates[b];
+              const uint32_t* in = args.payload + args.offsets[b];
+              const uint32_t target = dec_target(st);
+              CdfRow R;
+              cdf_prepare(src, args.inv_t, R);
+              uint32_t lo, hi;
+              const int s = cdf_search(src, R, target, lo, hi);
+              args.out_bytes[base + t] = (uint8_t)s;
+              dec_update(st, lo, hi, in);
+              args.dstates[b] = st;
+            }
+          }
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 3-D map over a [2][rows][K] bf16 plane pair, box = 64 (K) x box_rows x 1.
+static bool make_plane_map(CUtensorMap* map, const void* base, int K, int rows, long long plane, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, 2};
+  cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)plane * 2};
+  cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, int MODE>
+static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tw, const GemmArgs& a, cudaStream_t st) {
+  using Cfg = GemmCfg<BN>;
+  dim3 grid(a.N / BN, (a.M + kBM - 1) / kBM);
+  gemm_kernel<BN, MODE><<<grid, kThreads, Cfg::kSmem, st>>>(ta, tw, a);
+  return cudaGetLastError();
+}
+
+template <int BN, int MODE>
+static cudaError_t set_attr_t() {
+  return cudaFuncSetAttribute(gemm_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::kSmem);
+}
+
+template <int BN>
+static cudaError_t dispatch(int mode, const CUtensorMap& ta, const CUtensorMap& tw, const GemmArgs& a,
+                            cudaStream_t st) {
+  switch (mode) {
+    case EPI_F32: return launch_t<BN, EPI_F32>(ta, tw, a, st);
+    case EPI_ACT_SPLIT: return launch_t<BN, EPI_ACT_SPLIT>(ta, tw, a, st);
+    case EPI_LN_SPLIT: return launch_t<BN, EPI_LN_SPLIT>(ta, tw, a, st);
+    case EPI_RES_LN: return launch_t<BN, EPI_RES_LN>(ta, tw, a, st);
+    case EPI_LOGITS: return BN == 256 ? launch_t<BN, EPI_LOGITS>(ta, tw, a, st) : cudaErrorInvalidValue;
+    case EPI_HEAD_ENC: return BN == 256 ? launch_t<BN, EPI_HEAD_ENC>(ta, tw, a, st) : cudaErrorInvalidValue;
+    case EPI_HEAD_DEC: return BN == 256 ? launch_t<BN, EPI_HEAD_DEC>(ta, tw, a, st) : cudaErrorInvalidValue;
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <int BN>
+static cudaError_t set_attrs() {
+  cudaError_t e;
+  if ((e = set_attr_t<BN, EPI_F32>()) != cudaSuccess) return e;
+  if ((e = set_attr_t<BN, EPI_ACT_SPLIT>()) != cudaSuccess) return e;
+  if ((e = set_attr_t<BN, EPI_LN_SPLIT>()) != cudaSuccess) return e;
+  if ((e = set_attr_t<BN, EPI_RES_LN>()) != cudaSuccess) return e;
+  if (BN == 256) {
+    if ((e = set_attr_t<BN, EPI_LOGITS>()) != cudaSuccess) return e;
+    if ((e = set_attr_t<BN, EPI_HEAD_ENC>()) != cudaSuccess) return e;
+    if ((e = set_attr_t<BN, EPI_HEAD_DEC>()) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+// Once per device (current device), before any launch or stream capture:
+// opt the GEMM kernels into >48 KB dynamic shared memory and resolve the
+// tensor-map encoder.
+cudaError_t gemm_prepare_device() {
+  if (!get_encode_fn()) return cudaErrorNotSupported;
+  cudaError_t e;
+  if ((e = set_attrs<48>()) != cudaSuccess) return e;
+  if ((e = set_attrs<64>()) != cudaSuccess) return e;
+  if ((e = set_attrs<128>()) != cudaSuccess) return e;
+  return set_attrs<256>();
+}
+
+// CTA tile width: a full row for the row-wise epilogues (LayerNorm, coder),
+// 256 for wide outputs, else the (padded) width itself.
+static int pick_bn(int mode, int N) {
+  if (mode == EPI_LN_SPLIT || mode == EPI_RES_LN || mode >= EPI_LOGITS) return N;
+  if (N % 256 == 0) return 256;
+  return N;
+}
+
+cudaError_t gemm_launch(int mode, const __nv_bfloat16* A, long long a_plane, int /*unused*/,
+                        const __nv_bfloat16* W, long long w_plane, const GemmArgs& args, cudaStream_t stream) {
+  if (args.K % 16 != 0 || args.K <= 0 || args.M <= 0) return cudaErrorInvalidValue;
+  const int BN = pick_bn(mode, args.N);
+  if (BN != 48 && BN != 64 && BN != 128 && BN != 256) return cudaErrorInvalidValue;
+  if (mode >= EPI_LOGITS && BN != 256) return cudaErrorInvalidValue;
+  CUtensorMap ta, tw;
+  if (!make_plane_map(&ta, A, args.K, args.M, a_plane, kBM)) return cudaErrorInvalidValue;
+  if (!make_plane_map(&tw, W, args.K, args.N, w_plane, BN)) return cudaErrorInvalidValue;
+  switch (BN) {
+    case 48: return dispatch<48>(mode, ta, tw, args, stream);
+    case 64: return dispatch<64>(mode, ta, tw, args, stream);
+    case 128: return dispatch<128>(mode, ta, tw, args, stream);
+    default: return dispatch<256>(mode, ta, tw, args, stream);
+  }
+}
+
+}  // namespace boa

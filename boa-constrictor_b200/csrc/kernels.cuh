@@ -1,0 +1,78 @@
+// kernels.cuh -- launchers for the non-GEMM kernels of the compress/decompress
+// path (embedding + LayerNorm, causal conv, selective scan, range-coder
+// bookkeeping, integer-CDF coder).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include "coder.cuh"
+
+namespace boa {
+
+// Where each row's input token comes from.
+struct TokenSrc {
+  int mode;               // 0: tokens[row]; 1: compress tile; 2: decompress step
+  const uint8_t* bytes;   // mode 0: [M]; mode 1: batch input; mode 2: batch output
+  long long n_bytes;      // bytes from the batch's first chunk to the stream end
+  int chunk_len, t0, T;   // mode 1
+  const int* d_t;         // mode 2: current step; the token is byte t-1
+};
+
+// x[row] = E[token]; xn = split(LN(x; w, b))   (rows = M, width d)
+cudaError_t launch_embed_ln(const TokenSrc& src, const float* emb, int d, float* x, __nv_bfloat16* xn,
+                            long long xn_plane, const float* ln_w, const float* ln_b, int M,
+                            cudaStream_t st);
+
+// u = silu(causal_conv4(x)), x = xz[:, :di]; rows (b, tau) with T rows per
+// chunk; conv_state [B][3][di] holds the three previous inputs.
+cudaError_t launch_conv(const float* xz, int di, float* conv_state, const float* conv_w, const float* conv_b,
+                        float* u, __nv_bfloat16* uhl, long long plane, int B, int T, cudaStream_t st);
+
+// selective scan with fused dt_proj + softplus + D skip + SiLU(z) gate.
+// delta [M][ld_delta] = [dt_in(r) | B(16) | C(16)]; ssm_state [B][16][di].
+cudaError_t launch_scan(const float* delta, int ld_delta, int r, const float* dt_w, const float* dt_b,
+                        const float* negA, const float* Dv, const float* u, const float* xz, int di,
+                        float* ssm_state, __nv_bfloat16* yhl, long long plane, int B, int T, cudaStream_t st);
+
+// minGRU recurrence: h = (1-z) h + z g(ht) over T rows per chunk; writes h
+// into x_out rows (boa_gpu.hpp:652-693).  zh = [M][2d] (z logits | h~ raw).
+cudaError_t launch_mingru(const float* zh, int d, float* h_state, float* x_out, int B, int T, cudaStream_t st);
+
+// x += y (residual), then xn = split(LN(x)) -- minGRU blocks
+cudaError_t launch_add_ln(float* x, const float* y, int d, __nv_bfloat16* xn, long long plane,
+                          const float* ln_w, const float* ln_b, int M, cudaStream_t st);
+// final RMSNorm then split (minGRU head input)
+cudaError_t launch_rms_split(const float* x, int d, const float* w, __nv_bfloat16* xn, long long plane, int M,
+                             cudaStream_t st);
+
+// compress: encode one tile of (low, high) per chunk; lf [B][T]
+cudaError_t launch_encode_tile(const uint2* lf, EncState* es, uint32_t* pitch_buf, int pitch_words, int B,
+                               int T, int t0, long long n_bytes, int chunk_len, cudaStream_t st);
+cudaError_t launch_enc_init(EncState* es, int B, cudaStream_t st);
+cudaError_t launch_enc_finish(EncState* es, uint32_t* pitch_buf, int pitch_words, uint32_t* sizes, int B,
+                              cudaStream_t st);
+// exclusive scan of sizes -> offsets (one block); total in offsets[B]
+cudaError_t launch_offsets(const uint32_t* sizes, unsigned long long* offsets, int B, cudaStream_t st);
+cudaError_t launch_compact(const uint32_t* pitch_buf, int pitch_words, const uint32_t* sizes,
+                           const unsigned long long* offsets, uint32_t* payload, int B, cudaStream_t st);
+cudaError_t launch_first_bytes(const uint8_t* data, long long n_bytes, int chunk_len, uint8_t* first, int B,
+                               cudaStream_t st);
+// decompress
+cudaError_t launch_dec_init(DecState* ds, const uint32_t* payload, const unsigned long long* offsets,
+                            const uint32_t* sizes, const uint8_t* first, uint8_t* out, long long n_bytes,
+                            int chunk_len, int B, cudaStream_t st);
+cudaError_t launch_set_counter(int* d_t, int value, cudaStream_t st);
+cudaError_t launch_increment(int* d_t, cudaStream_t st);
+
+// integer-CDF coder (configs[1] style): cdf [n_steps][n_streams][257]
+cudaError_t launch_rc_encode_cdf(EncState* es, const uint32_t* cdf, const uint8_t* syms, int n_streams,
+                                 int n_steps, uint32_t* pitch_buf, int pitch_words, cudaStream_t st);
+cudaError_t launch_rc_decode_init(DecState* ds, const uint32_t* payload, const unsigned long long* offsets,
+                                  const uint32_t* sizes, int n_streams, cudaStream_t st);
+cudaError_t launch_rc_decode_cdf(DecState* ds, const uint32_t* cdf, const uint32_t* payload,
+                                 const unsigned long long* offsets, int n_streams, int n_steps, uint8_t* syms,
+                                 cudaStream_t st);
+// CDF of logits rows (test hook for the shared CDF code): Q [rows][257]
+cudaError_t launch_cdf_rows(const float* logits, int rows, float inv_t, uint32_t* Q, cudaStream_t st);
+
+}  // namespace boa

@@ -1,0 +1,506 @@
+// mamba.cu -- non-GEMM kernels of the compress/decompress step.
+//
+// Row layout: rows are (chunk b, position tau) with T rows per chunk; the
+// decompress step is the T = 1 case of the same kernels, so both directions
+// run identical arithmetic per row.
+#include "kernels.cuh"
+
+namespace boa {
+
+// ---------------------------------------------------------------- helpers
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ int chunk_len_of(long long n_bytes, int chunk_len, int b) {
+  const long long rem = n_bytes - (long long)b * chunk_len;
+  return (int)(rem < chunk_len ? (rem > 0 ? rem : 0) : chunk_len);
+}
+
+// ---------------------------------------------------------------- embedding + LN
+// One warp per row, D/32 values per lane.  Restates the embedding gather
+// (utility_kernels.cu:46-72) and LN1 (inference_kernels.cu:293-348).
+template <int D>
+__global__ void embed_ln_kernel(TokenSrc src, const float* __restrict__ emb, float* __restrict__ x,
+                                __nv_bfloat16* __restrict__ xn, long long plane, const float* __restrict__ w,
+                                const float* __restrict__ bb, int M) {
+  constexpr int V = D / 32;
+  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  int tok = 0;
+  if (src.mode == 0) {
+    tok = src.bytes[row];
+  } else if (src.mode == 1) {
+    const int b = row / src.T, tau = row - b * src.T;
+    const int p = src.t0 + tau;
+    if (p < chunk_len_of(src.n_bytes, src.chunk_len, b)) tok = src.bytes[(long long)b * src.chunk_len + p];
+  } else {
+    const int b = row;
+    const int p = *src.d_t - 1;
+    if (p >= 0 && p < chunk_len_of(src.n_bytes, src.chunk_len, b)) tok = src.bytes[(long long)b * src.chunk_len + p];
+  }
+  float v[V];
+  float s = 0.f, sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    v[i] = emb[(size_t)tok * D + lane + 32 * i];
+    x[(size_t)row * D + lane + 32 * i] = v[i];
+    s += v[i];
+    sq += v[i] * v[i];
+  }
+  s = warp_sum(s);
+  sq = warp_sum(sq);
+  const float mean = s / (float)D;
+  const float var = sq / (float)D - mean * mean;
+  const float inv_std = rsqrtf(var + 1e-5f);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = lane + 32 * i;
+    const float y = (v[i] - mean) * inv_std * w[c] + bb[c];
+    __nv_bfloat16 h, l;
+    split_bf16(y, h, l);
+    xn[(size_t)row * D + c] = h;
+    xn[plane + (size_t)row * D + c] = l;
+  }
+}
+
+cudaError_t launch_embed_ln(const TokenSrc& src, const float* emb, int d, float* x, __nv_bfloat16* xn,
+                            long long plane, const float* w, const float* b, int M, cudaStream_t st) {
+  const int rows_per_block = 8;
+  dim3 grid((M + rows_per_block - 1) / rows_per_block), block(32 * rows_per_block);
+  switch (d) {
+    case 64: embed_ln_kernel<64><<<grid, block, 0, st>>>(src, emb, x, xn, plane, w, b, M); break;
+    case 128: embed_ln_kernel<128><<<grid, block, 0, st>>>(src, emb, x, xn, plane, w, b, M); break;
+    case 256: embed_ln_kernel<256><<<grid, block, 0, st>>>(src, emb, x, xn, plane, w, b, M); break;
+    case 512: embed_ln_kernel<512><<<grid, block, 0, st>>>(src, emb, x, xn, plane, w, b, M); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- causal conv
+// Thread per (chunk, channel); window = three carried inputs + current.
+// Sum order bias, oldest tap .. newest (mamba_kernels.cu:158-197, :370-412).
+__global__ void conv_kernel(const float* __restrict__ xz, int di, float* __restrict__ cst,
+                            const float* __restrict__ cw, const float* __restrict__ cb, float* __restrict__ u,
+                            __nv_bfloat16* __restrict__ uhl, long long plane, int B, int T) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)B * di) return;
+  const int b = (int)(idx / di), c = (int)(idx - (long long)b * di);
+  float* s = cst + (size_t)b * 3 * di + c;
+  float w0 = s[0], w1 = s[di], w2 = s[2 * di];
+  const float4 k = reinterpret_cast<const float4*>(cw)[c];
+  const float bias = cb[c];
+  for (int tau = 0; tau < T; ++tau) {
+    const size_t row = (size_t)b * T + tau;
+    const float xt = xz[row * 2 * di + c];
+    float v = bias;
+    v = v + w0 * k.x;
+    v = v + w1 * k.y;
+    v = v + w2 * k.z;
+    v = v + xt * k.w;
+    const float o = v / (1.0f + expf(-v));
+    u[row * di + c] = o;
+    __nv_bfloat16 h, l;
+    split_bf16(o, h, l);
+    uhl[row * di + c] = h;
+    uhl[plane + row * di + c] = l;
+    w0 = w1; w1 = w2; w2 = xt;
+  }
+  s[0] = w0; s[di] = w1; s[2 * di] = w2;
+}
+
+cudaError_t launch_conv(const float* xz, int di, float* cst, const float* cw, const float* cb, float* u,
+                        __nv_bfloat16* uhl, long long plane, int B, int T, cudaStream_t st) {
+  const long long n = (long long)B * di;
+  conv_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(xz, di, cst, cw, cb, u, uhl, plane, B, T);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- selective scan
+// Thread per (chunk, channel), state h[16] in registers across the T rows.
+// dt = softplus(delta[:r] . Wdt[c] + b) restates dt_proj + softplus
+// (inference_kernels.cu:372-390); the recurrence restates
+// mamba_kernels.cu:271-361 / :414-470; the gate mamba_kernels.cu:130-151.
+template <int R>
+__global__ void __launch_bounds__(128) scan_kernel(const float* __restrict__ delta, int ld, const float* __restrict__ dtw,
+                                                   const float* __restrict__ dtb, const float* __restrict__ negA,
+                                                   const float* __restrict__ Dv, const float* __restrict__ u,
+                                                   const float* __restrict__ xz, int di, float* __restrict__ hs,
+                                                   __nv_bfloat16* __restrict__ yhl, long long plane, int T) {
+  extern __shared__ float sdelta[];  // [T][ld]
+  const int b = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  for (int i = threadIdx.x; i < T * ld; i += blockDim.x) sdelta[i] = delta[(size_t)b * T * ld + i];
+  __syncthreads();
+  if (c >= di) return;
+  float wdt[R];
+#pragma unroll
+  for (int k = 0; k < R; ++k) wdt[k] = dtw[(size_t)c * R + k];
+  float na[16], h[16];
+  float* hp = hs + (size_t)b * 16 * di + c;
+#pragma unroll
+  for (int n = 0; n < 16; ++n) { na[n] = negA[(size_t)c * 16 + n]; h[n] = hp[(size_t)n * di]; }
+  const float bdt = dtb[c], dsk = Dv[c];
+  for (int tau = 0; tau < T; ++tau) {
+    const float* dl = sdelta + tau * ld;
+    const size_t row = (size_t)b * T + tau;
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < R; ++k) acc = fmaf(dl[k], wdt[k], acc);
+    const float dt = logf(1.0f + expf(acc + bdt));
+    const float uv = u[row * di + c];
+    float y = 0.f;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      const float dA = __expf(na[n] * dt);
+      const float dB = dt * dl[R + n];
+      h[n] = dA * h[n] + dB * uv;
+      y = y + h[n] * dl[R + 16 + n];
+    }
+    y = y + uv * dsk;
+    const float z = xz[row * 2 * di + di + c];
+    const float o = y * (z / (1.0f + expf(-z)));
+    __nv_bfloat16 hh, ll;
+    split_bf16(o, hh, ll);
+    yhl[row * di + c] = hh;
+    yhl[plane + row * di + c] = ll;
+  }
+#pragma unroll
+  for (int n = 0; n < 16; ++n) hp[(size_t)n * di] = h[n];
+}
+
+cudaError_t launch_scan(const float* delta, int ld, int r, const float* dtw, const float* dtb, const float* negA,
+                        const float* Dv, const float* u, const float* xz, int di, float* hs, __nv_bfloat16* yhl,
+                        long long plane, int B, int T, cudaStream_t st) {
+  dim3 block(128), grid((di + 127) / 128, B);
+  const size_t sm = (size_t)T * ld * sizeof(float);
+  if (sm > 200 * 1024) return cudaErrorInvalidValue;
+  switch (r) {
+#define BOA_SCAN_CASE(RR)                                                                                     \
+  case RR:                                                                                                    \
+    if (sm > 48 * 1024) cudaFuncSetAttribute(scan_kernel<RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm); \
+    scan_kernel<RR><<<grid, block, sm, st>>>(delta, ld, dtw, dtb, negA, Dv, u, xz, di, hs, yhl, plane, T);     \
+    break;
+    BOA_SCAN_CASE(4)
+    BOA_SCAN_CASE(8)
+    BOA_SCAN_CASE(16)
+    BOA_SCAN_CASE(32)
+#undef BOA_SCAN_CASE
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- minGRU
+__global__ void mingru_kernel(const float* __restrict__ zh, int d, float* __restrict__ hstate,
+                              float* __restrict__ xo, int B, int T) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)B * d) return;
+  const int b = (int)(idx / d), c = (int)(idx - (long long)b * d);
+  float h = hstate[idx];
+  for (int tau = 0; tau < T; ++tau) {
+    const size_t row = (size_t)b * T + tau;
+    const float z = 1.0f / (1.0f + expf(-zh[row * 2 * d + c]));
+    const float hr = zh[row * 2 * d + d + c];
+    const float ht = hr >= 0.f ? hr + 0.5f : 1.0f / (1.0f + expf(-hr));
+    h = (1.0f - z) * h + z * ht;
+    xo[row * d + c] = h;
+  }
+  hstate[idx] = h;
+}
+cudaError_t launch_mingru(const float* zh, int d, float* hs, float* xo, int B, int T, cudaStream_t st) {
+  const long long n = (long long)B * d;
+  mingru_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(zh, d, hs, xo, B, T);
+  return cudaGetLastError();
+}
+
+template <int D, bool RMS>
+__global__ void add_ln_kernel(float* __restrict__ x, const float* __restrict__ y, __nv_bfloat16* __restrict__ xn,
+                              long long plane, const float* __restrict__ w, const float* __restrict__ bb, int M) {
+  constexpr int V = D / 32;
+  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  float v[V];
+  float s = 0.f, sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const size_t o = (size_t)row * D + lane + 32 * i;
+    float t = x[o];
+    if (y) { t = y[o] + t; x[o] = t; }
+    v[i] = t; s += t; sq += t * t;
+  }
+  s = warp_sum(s);
+  sq = warp_sum(sq);
+  float mean = 0.f, inv;
+  if (RMS) {
+    inv = rsqrtf(sq / (float)D + 1e-6f);
+  } else {
+    mean = s / (float)D;
+    inv = rsqrtf(sq / (float)D - mean * mean + 1e-5f);
+  }
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = lane + 32 * i;
+    const float o = RMS ? v[i] * inv * w[c] : (v[i] - mean) * inv * w[c] + bb[c];
+    __nv_bfloat16 h, l;
+    split_bf16(o, h, l);
+    xn[(size_t)row * D + c] = h;
+    xn[plane + (size_t)row * D + c] = l;
+  }
+}
+template <bool RMS>
+static cudaError_t launch_add_ln_t(float* x, const float* y, int d, __nv_bfloat16* xn, long long plane,
+                                   const float* w, const float* b, int M, cudaStream_t st) {
+  dim3 grid((M + 7) / 8), block(256);
+  switch (d) {
+    case 64: add_ln_kernel<64, RMS><<<grid, block, 0, st>>>(x, y, xn, plane, w, b, M); break;
+    case 128: add_ln_kernel<128, RMS><<<grid, block, 0, st>>>(x, y, xn, plane, w, b, M); break;
+    case 256: add_ln_kernel<256, RMS><<<grid, block, 0, st>>>(x, y, xn, plane, w, b, M); break;
+    case 512: add_ln_kernel<512, RMS><<<grid, block, 0, st>>>(x, y, xn, plane, w, b, M); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+cudaError_t launch_add_ln(float* x, const float* y, int d, __nv_bfloat16* xn, long long plane, const float* w,
+                          const float* b, int M, cudaStream_t st) {
+  return launch_add_ln_t<false>(x, y, d, xn, plane, w, b, M, st);
+}
+cudaError_t launch_rms_split(const float* x, int d, const float* w, __nv_bfloat16* xn, long long plane, int M,
+                             cudaStream_t st) {
+  return launch_add_ln_t<true>(const_cast<float*>(x), nullptr, d, xn, plane, w, nullptr, M, st);
+}
+
+// ---------------------------------------------------------------- range coder bookkeeping
+__global__ void enc_init_kernel(EncState* es, int B) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < B) enc_init(es[b]);
+}
+cudaError_t launch_enc_init(EncState* es, int B, cudaStream_t st) {
+  enc_init_kernel<<<(B + 255) / 256, 256, 0, st>>>(es, B);
+  return cudaGetLastError();
+}
+
+// Thread per chunk: encodes positions t0..t0+T-1 whose next byte exists
+// (encode loop of range_coder_kernels.cu:856-966 with the CDF already reduced
+// to (low, high) by the head epilogue).
+__global__ void encode_tile_kernel(const uint2* __restrict__ lf, EncState* es, uint32_t* pitch_buf, int pitch,
+                                   int B, int T, int t0, long long n_bytes, int chunk_len) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int len = chunk_len_of(n_bytes, chunk_len, b);
+  int n = len - 1 - t0;
+  if (n <= 0) return;
+  if (n > T) n = T;
+  EncState s = es[b];
+  uint32_t* out = pitch_buf + (size_t)b * pitch;
+  const uint2* p = lf + (size_t)b * T;
+  for (int i = 0; i < n; ++i) {
+    const uint2 v = p[i];
+    if (!enc_symbol(s, v.x, v.y - v.x, out, pitch)) { set_dev_error(BOA_ERR_STREAM_OVERFLOW); break; }
+  }
+  es[b] = s;
+}
+cudaError_t launch_encode_tile(const uint2* lf, EncState* es, uint32_t* pitch_buf, int pitch, int B, int T, int t0,
+                               long long n_bytes, int chunk_len, cudaStream_t st) {
+  encode_tile_kernel<<<(B + 127) / 128, 128, 0, st>>>(lf, es, pitch_buf, pitch, B, T, t0, n_bytes, chunk_len);
+  return cudaGetLastError();
+}
+
+__global__ void enc_finish_kernel(EncState* es, uint32_t* pitch_buf, int pitch, uint32_t* sizes, int B) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  EncState s = es[b];
+  const int w = enc_finish(s, pitch_buf + (size_t)b * pitch, pitch);
+  if (w < 0) set_dev_error(BOA_ERR_STREAM_OVERFLOW);
+  sizes[b] = w < 0 ? 0u : (uint32_t)w;
+  es[b] = s;
+}
+cudaError_t launch_enc_finish(EncState* es, uint32_t* pitch_buf, int pitch, uint32_t* sizes, int B, cudaStream_t st) {
+  enc_finish_kernel<<<(B + 255) / 256, 256, 0, st>>>(es, pitch_buf, pitch, sizes, B);
+  return cudaGetLastError();
+}
+
+// single-block exclusive scan; offsets[B] = total
+__global__ void offsets_kernel(const uint32_t* sizes, unsigned long long* off, int B) {
+  __shared__ unsigned long long part[1024];
+  const int t = threadIdx.x, nt = blockDim.x;
+  const unsigned long long base = off[0];  // running total of earlier batches
+  const int per = (B + nt - 1) / nt;
+  const int lo = t * per, hi = min(B, lo + per);
+  unsigned long long s = 0;
+  for (int i = lo; i < hi; ++i) s += sizes[i];
+  part[t] = s;
+  __syncthreads();
+  if (t == 0) {
+    unsigned long long run = base;
+    for (int i = 0; i < nt; ++i) { const unsigned long long v = part[i]; part[i] = run; run += v; }
+    off[B] = run;
+  }
+  __syncthreads();
+  unsigned long long run = part[t];
+  for (int i = lo; i < hi; ++i) { off[i] = run; run += sizes[i]; }
+}
+cudaError_t launch_offsets(const uint32_t* sizes, unsigned long long* off, int B, cudaStream_t st) {
+  offsets_kernel<<<1, 1024, 0, st>>>(sizes, off, B);
+  return cudaGetLastError();
+}
+
+__global__ void compact_kernel(const uint32_t* __restrict__ pitch_buf, int pitch, const uint32_t* __restrict__ sizes,
+                               const unsigned long long* __restrict__ off, uint32_t* __restrict__ payload) {
+  const int b = blockIdx.x;
+  const uint32_t n = sizes[b];
+  const uint32_t* src = pitch_buf + (size_t)b * pitch;
+  uint32_t* dst = payload + off[b];
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+}
+cudaError_t launch_compact(const uint32_t* pitch_buf, int pitch, const uint32_t* sizes,
+                           const unsigned long long* off, uint32_t* payload, int B, cudaStream_t st) {
+  compact_kernel<<<B, 256, 0, st>>>(pitch_buf, pitch, sizes, off, payload);
+  return cudaGetLastError();
+}
+
+__global__ void first_bytes_kernel(const uint8_t* data, long long n_bytes, int chunk_len, uint8_t* first, int B) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  first[b] = chunk_len_of(n_bytes, chunk_len, b) > 0 ? data[(long long)b * chunk_len] : 0;
+}
+cudaError_t launch_first_bytes(const uint8_t* data, long long n_bytes, int chunk_len, uint8_t* first, int B,
+                               cudaStream_t st) {
+  first_bytes_kernel<<<(B + 255) / 256, 256, 0, st>>>(data, n_bytes, chunk_len, first, B);
+  return cudaGetLastError();
+}
+
+// decoder init (range_coder_kernels.cu:319-335) + raw first byte (:792-826)
+__global__ void dec_init_kernel(DecState* ds, const uint32_t* payload, const unsigned long long* off,
+                                const uint32_t* sizes, const uint8_t* first, uint8_t* out, long long n_bytes,
+                                int chunk_len, int B) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  DecState s;
+  dec_init(s, payload + off[b], (int)sizes[b]);
+  ds[b] = s;
+  if (first && chunk_len_of(n_bytes, chunk_len, b) > 0) out[(long long)b * chunk_len] = first[b];
+}
+cudaError_t launch_dec_init(DecState* ds, const uint32_t* payload, const unsigned long long* off, const uint32_t* sizes,
+                            const uint8_t* first, uint8_t* out, long long n_bytes, int chunk_len, int B,
+                            cudaStream_t st) {
+  dec_init_kernel<<<(B + 255) / 256, 256, 0, st>>>(ds, payload, off, sizes, first, out, n_bytes, chunk_len, B);
+  return cudaGetLastError();
+}
+cudaError_t launch_rc_decode_init(DecState* ds, const uint32_t* payload, const unsigned long long* off,
+                                  const uint32_t* sizes, int n, cudaStream_t st) {
+  dec_init_kernel<<<(n + 255) / 256, 256, 0, st>>>(ds, payload, off, sizes, nullptr, nullptr, 0, 1, n);
+  return cudaGetLastError();
+}
+
+__global__ void set_counter_kernel(int* d_t, int v) { *d_t = v; }
+__global__ void increment_kernel(int* d_t) { *d_t += 1; }
+cudaError_t launch_set_counter(int* d_t, int v, cudaStream_t st) {
+  set_counter_kernel<<<1, 1, 0, st>>>(d_t, v);
+  return cudaGetLastError();
+}
+cudaError_t launch_increment(int* d_t, cudaStream_t st) {
+  increment_kernel<<<1, 1, 0, st>>>(d_t);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- integer-CDF coder
+// Encoder: thread per stream reads only Q[s] and Q[s+1] of each step.
+__global__ void rc_encode_cdf_kernel(EncState* es, const uint32_t* __restrict__ cdf, const uint8_t* __restrict__ syms,
+                                     int n_streams, int n_steps, uint32_t* pitch_buf, int pitch) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_streams) return;
+  EncState s = es[i];
+  uint32_t* out = pitch_buf + (size_t)i * pitch;
+  for (int t = 0; t < n_steps; ++t) {
+    const size_t rowi = (size_t)t * n_streams + i;
+    const int sym = syms[rowi];
+    const uint32_t* q = cdf + rowi * 257;
+    const uint32_t lo = q[sym], hi = q[sym + 1];
+    if (!enc_symbol(s, lo, hi - lo, out, pitch)) { set_dev_error(BOA_ERR_STREAM_OVERFLOW); break; }
+  }
+  es[i] = s;
+}
+cudaError_t launch_rc_encode_cdf(EncState* es, const uint32_t* cdf, const uint8_t* syms, int n_streams, int n_steps,
+                                 uint32_t* pitch_buf, int pitch, cudaStream_t st) {
+  rc_encode_cdf_kernel<<<(n_streams + 127) / 128, 128, 0, st>>>(es, cdf, syms, n_streams, n_steps, pitch_buf, pitch);
+  return cudaGetLastError();
+}
+
+// Decoder: one warp per stream.  Lane l reads Q[8l .. 8l+8] (coalesced
+// 1 KB row), tests its 8 symbols, and a ballot picks the lowest match, as the
+// reference's warp search does (range_coder_kernels.cu:743-763).  The coder
+// state is kept warp-uniform (every lane applies the same update).
+__global__ void rc_decode_cdf_kernel(DecState* ds, const uint32_t* __restrict__ cdf, const uint32_t* __restrict__ payload,
+                                     const unsigned long long* __restrict__ off, int n_streams, int n_steps,
+                                     uint8_t* __restrict__ syms) {
+  const int i = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (i >= n_streams) return;
+  DecState s = ds[i];
+  const uint32_t* in = payload + off[i];
+  for (int t = 0; t < n_steps; ++t) {
+    const size_t rowi = (size_t)t * n_streams + i;
+    const uint32_t* q = cdf + rowi * 257;
+    uint32_t v[9];
+#pragma unroll
+    for (int j = 0; j < 9; ++j) v[j] = q[lane * 8 + j];  // Q[256] read by lane 31 only is the total
+    const uint32_t target = dec_target(s);
+    int hit = -1;
+#pragma unroll
+    for (int j = 7; j >= 0; --j)
+      if (target >= v[j] && target < v[j + 1]) hit = j;
+    const unsigned ball = __ballot_sync(0xffffffffu, hit >= 0);
+    int sym = 0;
+    uint32_t lo = 0, hi = 0;
+    if (ball) {
+      const int wl = __ffs(ball) - 1;
+      sym = wl * 8 + __shfl_sync(0xffffffffu, hit, wl);
+      lo = q[sym];
+      hi = q[sym + 1];
+    }
+    if (lane == 0) syms[rowi] = (uint8_t)sym;
+    dec_update(s, lo, hi, in);
+  }
+  if (lane == 0) ds[i] = s;
+}
+cudaError_t launch_rc_decode_cdf(DecState* ds, const uint32_t* cdf, const uint32_t* payload,
+                                 const unsigned long long* off, int n_streams, int n_steps, uint8_t* syms,
+                                 cudaStream_t st) {
+  rc_decode_cdf_kernel<<<(n_streams + 7) / 8, 256, 0, st>>>(ds, cdf, payload, off, n_streams, n_steps, syms);
+  return cudaGetLastError();
+}
+
+// test hook: CDF of logits rows with the shared CDF code (one thread per row)
+struct GlobalRow {
+  const float* p;
+  __device__ __forceinline__ void lane(int l, float (&v)[8]) const {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = p[l * 8 + i];
+  }
+};
+__global__ void cdf_rows_kernel(const float* lg, int rows, float inv_t, uint32_t* Q) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  GlobalRow src{lg + (size_t)r * 256};
+  CdfRow R;
+  cdf_prepare(src, inv_t, R);
+  uint32_t* q = Q + (size_t)r * 257;
+  for (int s = 0; s < 256; ++s) {
+    uint32_t lo, hi;
+    cdf_symbol(src, R, s, lo, hi);
+    q[s] = lo;
+    if (s == 255) q[256] = hi;
+  }
+}
+cudaError_t launch_cdf_rows(const float* lg, int rows, float inv_t, uint32_t* Q, cudaStream_t st) {
+  cdf_rows_kernel<<<(rows + 63) / 64, 64, 0, st>>>(lg, rows, inv_t, Q);
+  return cudaGetLastError();
+}
+
+}  // namespace boa

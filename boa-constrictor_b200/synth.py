@@ -1,0 +1,151 @@
+"""Seeded synthetic inputs for the BoaConstrictor hot path.
+
+* ``write_random_weights`` writes a random-initialised model in the exact
+  ``.bin`` layout produced by the reference exporter
+  (portability_solved_cpp/convert_boa_weights.py:153-241, read back by
+  boa_gpu.hpp:990-1029): ``"BOA\\0"`` magic, embedding, per block ln1,
+  backbone, ln2, ff, then ``final_norm`` (non-Mamba backbones) and the head.
+  Every tensor is drawn in file order from one ``numpy.random.default_rng(seed)``
+  stream as N(0, 0.02), except LayerNorm/RMSNorm weights (= 1), LayerNorm
+  biases (= 0), ``A_log[c][n] = log(n + 1)`` and ``D = 1``; those fixed tensors
+  draw nothing from the stream.
+* ``particle_stream`` produces little-endian float32 records of 8 fields
+  (pT, eta, phi, mass, charge, three rounded N(0,1) covariates), drawn
+  field-major per block of 2**20 records from ``default_rng(seed)``.
+
+The reference ships no dataset for this path; these generators stand in for
+the CMS particle data its experiments use.
+"""
+from __future__ import annotations
+
+import math
+import numpy as np
+
+MAGIC_FP32 = b"BOA\x00"
+MAGIC_FP16 = b"BOA\x01"
+
+BACKBONES = {"mamba": 0, "mambav1": 0, "lstm": 1, "gru": 2, "mingru": 3}
+
+
+def mamba_dims(d_model: int):
+    """(d_inner, dt_rank, d_state) as MambaConfig computes them (gemm_gpu.hpp:57-65)."""
+    return 2 * d_model, (d_model + 15) // 16, 16
+
+
+def weight_tensors(backbone: str, d_model: int, n_layers: int):
+    """Yield (name, shape, kind) in file order; kind in {'rand','one','zero','alog','D'}."""
+    d = d_model
+    yield ("embedding.weight", (256, d), "rand")
+    for i in range(n_layers):
+        p = f"blocks.{i}."
+        yield (p + "ln1.weight", (d,), "one")
+        yield (p + "ln1.bias", (d,), "zero")
+        if BACKBONES[backbone] == 0:
+            di, r, ds = mamba_dims(d)
+            m = p + "mamba."
+            yield (m + "in_proj.weight", (2 * di, d), "rand")
+            yield (m + "in_proj.bias", (2 * di,), "rand")
+            yield (m + "conv1d.weight", (di, 1, 4), "rand")
+            yield (m + "conv1d.bias", (di,), "rand")
+            yield (m + "x_proj.weight", (r + 2 * ds, di), "rand")
+            yield (m + "dt_proj.weight", (di, r), "rand")
+            yield (m + "dt_proj.bias", (di,), "rand")
+            yield (m + "A_log", (di, ds), "alog")
+            yield (m + "D", (di,), "D")
+            yield (m + "out_proj.weight", (d, di), "rand")
+            yield (m + "out_proj.bias", (d,), "rand")
+        elif BACKBONES[backbone] == 3:
+            m = p + "mingru."
+            yield (m + "linear_z.weight", (d, d), "rand")
+            yield (m + "linear_z.bias", (d,), "rand")
+            yield (m + "linear_h.weight", (d, d), "rand")
+            yield (m + "linear_h.bias", (d,), "rand")
+        else:
+            raise ValueError(f"backbone {backbone!r} is not on this path")
+        yield (p + "ln2.weight", (d,), "one")
+        yield (p + "ln2.bias", (d,), "zero")
+        yield (p + "ff.0.weight", (4 * d, d), "rand")
+        yield (p + "ff.0.bias", (4 * d,), "rand")
+        yield (p + "ff.2.weight", (d, 4 * d), "rand")
+        yield (p + "ff.2.bias", (d,), "rand")
+    if BACKBONES[backbone] != 0:
+        yield ("final_norm.weight", (d,), "one")
+    yield ("head.0.weight", (d, d), "rand")
+    yield ("head.0.bias", (d,), "rand")
+    yield ("head.2.weight", (256, d), "rand")
+    yield ("head.2.bias", (256,), "rand")
+
+
+def random_weights(backbone: str, d_model: int, n_layers: int, seed: int, std: float = 0.02):
+    """Return an ordered list of (name, float32 array) for a random-init model."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for name, shape, kind in weight_tensors(backbone, d_model, n_layers):
+        if kind == "rand":
+            a = rng.normal(0.0, std, size=shape)
+        elif kind == "one":
+            a = np.ones(shape)
+        elif kind == "zero":
+            a = np.zeros(shape)
+        elif kind == "alog":
+            a = np.broadcast_to(np.log(np.arange(1, shape[1] + 1, dtype=np.float64)), shape)
+        elif kind == "D":
+            a = np.ones(shape)
+        else:  # pragma: no cover
+            raise AssertionError(kind)
+        out.append((name, np.ascontiguousarray(a, dtype=np.float32)))
+    return out
+
+
+def write_weights(path: str, tensors, fp16: bool = False) -> int:
+    """Write (name, array) pairs in order with the BOA header; returns bytes written."""
+    with open(path, "wb") as f:
+        f.write(MAGIC_FP16 if fp16 else MAGIC_FP32)
+        for _, a in tensors:
+            f.write((a.astype(np.float16) if fp16 else a.astype(np.float32)).tobytes())
+        return f.tell()
+
+
+def write_random_weights(path: str, backbone: str = "mamba", d_model: int = 256,
+                         n_layers: int = 8, seed: int = 0, fp16: bool = False) -> int:
+    return write_weights(path, random_weights(backbone, d_model, n_layers, seed), fp16=fp16)
+
+
+def particle_stream(n_bytes: int, seed: int) -> bytes:
+    """Little-endian float32 particle records (8 fields, 32 bytes each)."""
+    rng = np.random.default_rng(seed)
+    n_rec = (n_bytes + 31) // 32
+    blocks = []
+    for start in range(0, n_rec, 1 << 20):
+        nb = min(1 << 20, n_rec - start)
+        pt = rng.exponential(30.0, nb)
+        eta = rng.uniform(-2.5, 2.5, nb)
+        phi = rng.uniform(-math.pi, math.pi, nb)
+        mass = np.abs(rng.normal(0.14, 0.05, nb))
+        charge = rng.integers(0, 2, nb) * 2 - 1
+        cov = np.round(rng.normal(0.0, 1.0, (3, nb)), 3)
+        rec = np.stack([pt, eta, phi, mass, charge, cov[0], cov[1], cov[2]], axis=1)
+        blocks.append(rec.astype("<f4"))
+    data = np.concatenate(blocks).tobytes() if blocks else b""
+    return data[:n_bytes]
+
+
+def exact_logit_weights(d_model: int, n_layers: int, seed: int, support, low: float = -1000.0):
+    """Random-init Mamba model whose logits are exactly the head bias.
+
+    ``head.2.weight`` is zero and ``head.2.bias`` is 0 on ``support`` and
+    ``low`` elsewhere, so every position's logits are exact constants and the
+    softmax exponentials are exactly 1 or 0 on any IEEE machine.  The integer
+    CDF is then identical on CPU and GPU, which pins the quantiser, the range
+    coder and the container bit for bit against the reference binary.
+    """
+    ts = random_weights("mamba", d_model, n_layers, seed)
+    out = []
+    for name, a in ts:
+        if name == "head.2.weight":
+            a = np.zeros_like(a)
+        elif name == "head.2.bias":
+            a = np.full_like(a, low)
+            a[np.asarray(list(support), dtype=np.int64)] = 0.0
+        out.append((name, a))
+    return out

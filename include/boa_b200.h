@@ -1,0 +1,151 @@
+/*
+ * boa_b200.h -- C ABI of the B200-native BoaConstrictor compress/decompress
+ * library (libboa_b200.so).
+ *
+ * The reference (AkarshSahlot/boa-constrictor, portability_solved_cpp/) has no
+ * C ABI: its operator surface is C++ free functions on raw device pointers with
+ * a global stream and exit(1) on error (gemm_gpu.hpp:68-79, :124-265), driven
+ * by BoaPredictorGPU (boa_gpu.hpp:944-1174) and the CLI loops compress_v2 /
+ * decompress_v2 (boa.cpp:280-582, :584-817).  Each entry point below names the
+ * reference interface it replaces.  Conventions:
+ *   - every call returns 0 on success or a negative BOA_E_* code; the message
+ *     is available from boa_last_error();
+ *   - host pointers are caller-owned; device memory is owned by the handle;
+ *   - one handle drives one GPU; distinct handles may be used concurrently
+ *     from distinct host threads; a single handle is not re-entrant.
+ */
+#ifndef BOA_B200_H
+#define BOA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BOA_OK 0
+#define BOA_E_INVALID (-1)   /* bad argument */
+#define BOA_E_CUDA (-2)      /* CUDA runtime error (no GPU, launch failure, ...) */
+#define BOA_E_IO (-3)        /* file not readable / writable */
+#define BOA_E_FORMAT (-4)    /* weight file or container malformed */
+#define BOA_E_DEVICE (-5)    /* device-side check failed (wait timeout, stream overflow) */
+#define BOA_E_NOMEM (-6)     /* device allocation failed */
+
+#define BOA_BACKBONE_MAMBA 0 /* gemm_gpu.hpp BackboneType: mamba (mambav1 blocks) */
+#define BOA_BACKBONE_MINGRU 3
+
+typedef struct boa_model boa_model;
+
+/* ---- model --------------------------------------------------------------
+ * Replaces MambaConfig (gemm_gpu.hpp:38-66), the BoaPredictorGPU constructor
+ * and load_weights (boa_gpu.hpp:945-1029).  Reads the .bin layout of
+ * convert_boa_weights.py:153-241 ("BOA\0" fp32 or "BOA\1" fp16 header, or a
+ * headerless legacy fp32 file); d_model and n_layers are not stored in the
+ * file and must be given, as on the reference CLI (boa.cpp:912-919).  The
+ * file size must match the dims exactly (BOA_E_FORMAT otherwise). */
+int boa_model_load(const char* weights_path, int backbone, int d_model, int n_layers, int device,
+                   boa_model** out);
+/* Releases the handle and all its device memory (the reference never frees). */
+void boa_model_free(boa_model* h);
+/* Message of the last failed call on this handle (or of the last failed
+ * boa_model_load when h is NULL). */
+const char* boa_last_error(const boa_model* h);
+/* Replaces gpu_set_temperature (range_coder_kernels.cu:9-12): logits are
+ * scaled by 1/T (computed in fp32) before the softmax. */
+int boa_set_temperature(boa_model* h, float temperature);
+/* Replaces the global g_stream (utility_kernels.cu:5): work is ordered after
+ * prior work on `cuda_stream` and later work on it waits for the library.
+ * NULL restores the handle's private stream. */
+int boa_set_stream(boa_model* h, void* cuda_stream);
+/* Chunks per batch (--gpu-batch, boa.cpp:310) and tokens per compress tile
+ * (--tile, boa.cpp:313-316).  0 = automatic from free device memory
+ * (auto_size_params, boa.cpp:109-156). */
+int boa_set_batch(boa_model* h, int chunks_per_batch, int tile_tokens);
+/* Per-chunk stream capacity in 32-bit words used on the device for a chunk
+ * length (a tight bound: <= 24.01 bits per byte plus the flush words). */
+uint32_t boa_stream_capacity_words(uint32_t chunk_len);
+
+/* ---- host-buffer codec (the body of compress_v2 / decompress_v2) --------
+ * Chunk i of the stream covers data[i*chunk_len, min(n, (i+1)*chunk_len)).
+ * Compress chunks [first_chunk, first_chunk + n_chunks): writes the raw first
+ * byte of each chunk, each chunk's range-coded words concatenated in chunk
+ * order into payload (the BOA2 payload, boa.cpp:561-569) and the word count
+ * of each chunk into sizes_words.  *payload_words_out = total words.
+ * Returns BOA_E_INVALID if payload_cap_words is too small (nothing written). */
+int boa_compress_chunks(boa_model* h, const uint8_t* data, size_t n, uint32_t chunk_len, uint32_t first_chunk,
+                        uint32_t n_chunks, uint8_t* first_bytes, uint32_t* payload, size_t payload_cap_words,
+                        uint32_t* sizes_words, uint64_t* payload_words_out);
+/* Inverse: payload holds the n_chunks streams back to back with word counts
+ * sizes_words; chunk j (0-based within the call) decodes chunk_lens[j] bytes
+ * into out + j*chunk_len.  Replaces the decode loop of boa.cpp:672-774. */
+int boa_decompress_chunks(boa_model* h, const uint32_t* payload, const uint32_t* sizes_words,
+                          const uint8_t* first_bytes, const uint32_t* chunk_lens, uint32_t chunk_len,
+                          uint32_t n_chunks, uint8_t* out);
+
+/* ---- device-buffer codec (inputs already resident in HBM) ---------------
+ * Same as above on device pointers, enqueued asynchronously on the handle's
+ * stream.  n_bytes counts the bytes from chunk 0 of this call to the end of
+ * the stream, so chunk j has min(chunk_len, n_bytes - j*chunk_len) bytes.
+ * d_offsets has n_chunks + 1 entries (exclusive prefix of sizes; last =
+ * total).  Check boa_sync() before reading results. */
+int boa_compress_device(boa_model* h, const uint8_t* d_data, uint64_t n_bytes, uint32_t chunk_len,
+                        uint32_t n_chunks, uint8_t* d_first_bytes, uint32_t* d_payload, uint64_t payload_cap_words,
+                        uint32_t* d_sizes_words, uint64_t* d_offsets);
+int boa_decompress_device(boa_model* h, const uint32_t* d_payload, const uint64_t* d_offsets,
+                          const uint32_t* d_sizes_words, const uint8_t* d_first_bytes, uint64_t n_bytes,
+                          uint32_t chunk_len, uint32_t n_chunks, uint8_t* d_out);
+/* Waits for the handle's work and reports device-side failures. */
+int boa_sync(boa_model* h);
+/* Device memory the handle holds (weights + work buffers + states). */
+uint64_t boa_device_bytes(const boa_model* h);
+
+/* ---- model outputs for parity testing ------------------------------------
+ * Logits [B][L][256] (head bias included) of B fresh chunks of L tokens.
+ * mode 0 runs the compress form (all L positions per launch, as
+ * BoaPredictorGPU::forward_chunk, boa_gpu.hpp:1081-1102); mode 1 runs the
+ * decompress form (L single-position steps, as step_batch,
+ * boa_gpu.hpp:1034-1053).  Host buffers. */
+int boa_model_logits(boa_model* h, const uint8_t* tokens, int B, int L, int mode, float* logits);
+
+/* ---- range coder on explicit integer CDFs --------------------------------
+ * CDFs Q[n_steps][n_streams][257] (Q[s] = cumulative frequency of symbols
+ * below s, Q[256] = 2^24, strictly increasing), symbols [n_steps][n_streams].
+ * Replaces the coder of ker_rc_encode_chunk_parallel_warp / ker_rc_finish /
+ * ker_rc_init_decoder / ker_rc_decode_fused_step_warp
+ * (range_coder_kernels.cu:46-60, :279-335, :725-780, :916-968) for callers
+ * that supply the CDF.  Host buffers; streams are returned back to back like
+ * a BOA2 payload. */
+int boa_rc_encode_cdf(boa_model* h, const uint32_t* cdf, const uint8_t* syms, int n_streams, int n_steps,
+                      uint32_t* payload, size_t payload_cap_words, uint32_t* sizes_words);
+int boa_rc_decode_cdf(boa_model* h, const uint32_t* cdf, int n_streams, int n_steps, const uint32_t* payload,
+                      const uint32_t* sizes_words, uint8_t* syms);
+/* The integer CDF the library derives from one or more logits rows
+ * ([rows][256] -> [rows][257]); exposes the quantiser of
+ * range_coder_kernels.cu:860-925 for testing.  Host buffers. */
+int boa_cdf_from_logits(boa_model* h, const float* logits, int rows, float inv_temperature, uint32_t* cdf);
+
+/* ---- BOA2 container (boa.cpp:85-107, :158-277, :538-581) ----------------
+ * Serialises a container into buf (cap bytes); *len_out = bytes needed (call
+ * with buf = NULL to size).  flags bit0 = warm start; interleave_batch is
+ * written as the 4-byte fingerprint field when warm start is set. */
+int boa_boa2_build(uint64_t total_size, uint32_t chunk_len, uint32_t n_chunks, uint32_t last_chunk_len,
+                   uint32_t flags, uint32_t interleave_batch, const uint8_t* first_bytes,
+                   const uint64_t* stream_bytes, const uint8_t* payload, uint8_t* buf, size_t cap,
+                   size_t* len_out);
+typedef struct boa2_info {
+  uint64_t total_size;
+  uint32_t chunk_len, n_chunks, last_chunk_len, flags, interleave_batch;
+  uint32_t index_version; /* 1 or 2 */
+  uint64_t payload_offset, payload_bytes;
+} boa2_info;
+/* Parses and validates (magic, version, index, CRC-32, ranges).  first_bytes,
+ * offsets and lengths (bytes, relative to the payload) may be NULL to query
+ * info only; otherwise they need n_chunks entries. */
+int boa_boa2_parse(const uint8_t* buf, size_t len, boa2_info* info, uint8_t* first_bytes, uint64_t* offsets,
+                   uint64_t* lengths);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BOA_B200_H */

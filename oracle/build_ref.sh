@@ -1,0 +1,25 @@
+#!/usr/bin/env bash
+# Compiles the reference's own C++/CUDA path from its sources (read in place,
+# never copied) into oracle/_ref/:
+#   boa_constrictor  the reference CLI, portability_solved_cpp/README.md:11
+#                    build line plus an sm_100a target
+#   ref_logits       oracle/ref_harness.cu linked against the reference kernels
+# Needs the reference checkout (default /root/reference, or $BOA_REF_DIR);
+# without it the script does nothing and says so.  Outputs are git-ignored.
+set -euo pipefail
+HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
+REF="${BOA_REF_DIR:-/root/reference}/portability_solved_cpp"
+OUT="$HERE/_ref"
+if [ ! -f "$REF/boa.cpp" ]; then echo "reference sources not found at $REF; skipping"; exit 0; fi
+mkdir -p "$OUT"
+FLAGS=(-O3 -std=c++17 --fmad=false -DENABLE_GPU -DGPU_DEBUG_LOGITS=0 -DGPU_FAST_EXP=0
+       -gencode arch=compute_100a,code=sm_100a)
+KERNELS=("$REF/gemm_kernels.cu" "$REF/inference_kernels.cu" "$REF/mamba_kernels.cu"
+         "$REF/rnn_kernels.cu" "$REF/range_coder_kernels.cu" "$REF/utility_kernels.cu")
+if [ ! -x "$OUT/boa_constrictor" ] || [ "${FORCE:-0}" = 1 ]; then
+  nvcc -o "$OUT/boa_constrictor" "$REF/boa.cpp" "${KERNELS[@]}" "${FLAGS[@]}"
+fi
+if [ ! -x "$OUT/ref_logits" ] || [ "$HERE/ref_harness.cu" -nt "$OUT/ref_logits" ] || [ "${FORCE:-0}" = 1 ]; then
+  nvcc -o "$OUT/ref_logits" "$HERE/ref_harness.cu" "${KERNELS[@]}" -I"$REF" "${FLAGS[@]}"
+fi
+echo "reference build in $OUT"

@@ -1,0 +1,125 @@
+"""Generates the golden fixtures in tests/golden/ from the REFERENCE itself.
+
+Run on a GPU box (the reference is CUDA-only) after oracle/build_ref.sh has
+built oracle/_ref/{boa_constrictor,ref_logits} from the reference sources:
+
+    python tests/golden/make_golden.py <out_dir>
+
+Fixtures written (all inputs regenerate from the seeds recorded in
+manifest.json, so only reference OUTPUTS are stored):
+  ref_logits_<cfg>.npz   tokens + logits from BoaPredictorGPU::forward_chunk
+                         and ::step_batch (boa_gpu.hpp:1034, :1081)
+  ref_exact.boa          reference CLI compress of a seeded byte stream under
+                         an exact-logit model (synth.exact_logit_weights):
+                         pins quantiser + range coder + BOA2 container bit-exact
+  ref_rand_d256L8.boa    reference CLI compress of 64 KiB of particle records
+                         under the configs[0] model: container layout and the
+                         reference's bits/byte
+  manifest.json          parameters, sizes, sha256, reference round-trip flags
+"""
+import hashlib
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+REF = os.path.join(ROOT, "oracle", "_ref")
+spec = importlib.util.spec_from_file_location(
+    "synth", os.path.join(ROOT, "boa-constrictor_b200", "synth.py"))
+synth = importlib.util.module_from_spec(spec)
+spec.loader.exec_module(synth)
+
+EXACT = dict(d_model=64, n_layers=1, seed=7, support=list(range(0, 256, 5)) + [255],
+             n_bytes=4001, data_seed=11, chunk=1000, batch=8, p_out=0.05)
+LOGIT_CFGS = [dict(name="d64L2", d_model=64, n_layers=2, seed=3, B=3, T=40, tok_seed=5),
+              dict(name="d256L8", d_model=256, n_layers=8, seed=0, B=2, T=48, tok_seed=6)]
+RAND = dict(d_model=256, n_layers=8, seed=0, n_bytes=65536, data_seed=1, chunk=4096, batch=16)
+
+
+def exact_input(cfg):
+    """Bytes mostly from the support (exercise normal coding) and sometimes
+    outside it (frequency-1 symbols: long carry runs)."""
+    rng = np.random.default_rng(cfg["data_seed"])
+    sup = np.array(cfg["support"], np.uint8)
+    data = sup[rng.integers(0, len(sup), cfg["n_bytes"])]
+    out = rng.random(cfg["n_bytes"]) < cfg["p_out"]
+    data[out] = rng.integers(0, 256, int(out.sum()), dtype=np.uint8)
+    return data.tobytes()
+
+
+def sha(b):
+    return hashlib.sha256(b).hexdigest()
+
+
+def run(cmd):
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"{cmd} failed: {r.stdout[-2000:]} {r.stderr[-2000:]}")
+    return r.stdout
+
+
+def main(out_dir):
+    os.makedirs(out_dir, exist_ok=True)
+    tmp = os.path.join(out_dir, "_tmp")
+    os.makedirs(tmp, exist_ok=True)
+    man = {"exact": EXACT, "logits": LOGIT_CFGS, "rand": RAND}
+
+    for c in LOGIT_CFGS:
+        w = os.path.join(tmp, f"w_{c['name']}.bin")
+        synth.write_random_weights(w, "mamba", c["d_model"], c["n_layers"], c["seed"])
+        tok = np.random.default_rng(c["tok_seed"]).integers(0, 256, (c["B"], c["T"]), dtype=np.uint8)
+        tf = os.path.join(tmp, "tok.u8")
+        tok.tofile(tf)
+        res = {}
+        for mode in ("chunk", "step"):
+            of = os.path.join(tmp, f"lg_{mode}.f32")
+            run([os.path.join(REF, "ref_logits"), w, "mamba", str(c["d_model"]), str(c["n_layers"]),
+                 tf, str(c["B"]), str(c["T"]), mode, of])
+            res[mode] = np.fromfile(of, np.float32).reshape(c["B"], c["T"], 256)
+        np.savez_compressed(os.path.join(out_dir, f"ref_logits_{c['name']}.npz"),
+                            tokens=tok, chunk=res["chunk"], step=res["step"])
+
+    # exact-logit container
+    w = os.path.join(tmp, "w_exact.bin")
+    synth.write_weights(w, synth.exact_logit_weights(EXACT["d_model"], EXACT["n_layers"],
+                                                     EXACT["seed"], EXACT["support"]))
+    data = exact_input(EXACT)
+    fin = os.path.join(tmp, "exact.in"); open(fin, "wb").write(data)
+    boa = os.path.join(out_dir, "ref_exact.boa")
+    run([os.path.join(REF, "boa_constrictor"), "compress", w, fin, boa, str(EXACT["d_model"]),
+         str(EXACT["n_layers"]), "--gpu-batch", str(EXACT["batch"]), "--chunk-size", str(EXACT["chunk"])])
+    back = os.path.join(tmp, "exact.out")
+    run([os.path.join(REF, "boa_constrictor"), "decompress", w, boa, back, str(EXACT["d_model"]),
+         str(EXACT["n_layers"]), "--gpu-batch", str(EXACT["batch"])])
+    man["exact_result"] = dict(input_sha=sha(data), boa_bytes=os.path.getsize(boa),
+                               boa_sha=sha(open(boa, "rb").read()),
+                               ref_roundtrip=open(back, "rb").read() == data)
+
+    # random-init configs[0] model on particle records
+    w = os.path.join(tmp, "w_rand.bin")
+    synth.write_random_weights(w, "mamba", RAND["d_model"], RAND["n_layers"], RAND["seed"])
+    data = synth.particle_stream(RAND["n_bytes"], RAND["data_seed"])
+    fin = os.path.join(tmp, "rand.in"); open(fin, "wb").write(data)
+    boa = os.path.join(out_dir, "ref_rand_d256L8.boa")
+    run([os.path.join(REF, "boa_constrictor"), "compress", w, fin, boa, str(RAND["d_model"]),
+         str(RAND["n_layers"]), "--gpu-batch", str(RAND["batch"]), "--chunk-size", str(RAND["chunk"])])
+    back = os.path.join(tmp, "rand.out")
+    run([os.path.join(REF, "boa_constrictor"), "decompress", w, boa, back, str(RAND["d_model"]),
+         str(RAND["n_layers"]), "--gpu-batch", str(RAND["batch"])])
+    man["rand_result"] = dict(input_sha=sha(data), boa_bytes=os.path.getsize(boa),
+                              boa_sha=sha(open(boa, "rb").read()),
+                              bits_per_byte=8.0 * os.path.getsize(boa) / len(data),
+                              ref_roundtrip=open(back, "rb").read() == data)
+    for f in os.listdir(tmp):
+        os.remove(os.path.join(tmp, f))
+    os.rmdir(tmp)
+    json.dump(man, open(os.path.join(out_dir, "manifest.json"), "w"), indent=1)
+    print(json.dumps(man, indent=1))
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else os.path.join(ROOT, "tests", "golden"))
