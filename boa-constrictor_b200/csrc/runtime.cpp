@@ -228,13 +228,18 @@ void* ensure_io(boa_model* m, size_t bytes) {
   return m->io;
 }
 
+// Zero the recurrent state of chunks [0, B) in every layer.  Layer l's
+// slice starts at l * chunks_cap (the arrays are sized for the largest batch
+// seen), so each layer is cleared separately.
 int reset_states(boa_model* m, int B) {
-  const size_t n_conv = (size_t)m->L * B * 3 * m->di, n_ssm = (size_t)m->L * B * 16 * m->di;
-  if (m->backbone == BOA_BACKBONE_MAMBA) {
-    BOA_CK(cudaMemsetAsync(m->conv_st, 0, n_conv * 4, m->own));
-    BOA_CK(cudaMemsetAsync(m->ssm_st, 0, n_ssm * 4, m->own));
-  } else {
-    BOA_CK(cudaMemsetAsync(m->h_st, 0, (size_t)m->L * B * m->d * 4, m->own));
+  const size_t cap = m->chunks_cap;
+  for (int l = 0; l < m->L; ++l) {
+    if (m->backbone == BOA_BACKBONE_MAMBA) {
+      BOA_CK(cudaMemsetAsync(m->conv_st + (size_t)l * cap * 3 * m->di, 0, (size_t)B * 3 * m->di * 4, m->own));
+      BOA_CK(cudaMemsetAsync(m->ssm_st + (size_t)l * cap * 16 * m->di, 0, (size_t)B * 16 * m->di * 4, m->own));
+    } else {
+      BOA_CK(cudaMemsetAsync(m->h_st + (size_t)l * cap * m->d, 0, (size_t)B * m->d * 4, m->own));
+    }
   }
   return 0;
 }

@@ -1,0 +1,144 @@
+"""C-ABI host-side checks that need no GPU: the library loads, exports every
+symbol the header declares, validates inputs, and its BOA2 container code
+agrees byte for byte with the restatement and rejects damaged files."""
+import ctypes as C
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+
+
+def header_symbols(path):
+    src = open(path).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(boa_\w+)\s*\(", src, re.M)))
+
+
+def test_library_exports_every_declared_symbol(boa):
+    syms = header_symbols(boa.HEADER)
+    assert len(syms) >= 19
+    L = C.CDLL(boa.LIB_PATH)
+    missing = [s for s in syms if not hasattr(L, s)]
+    assert not missing
+    assert set(syms) == set(boa.SIGNATURES)
+
+
+def test_library_has_no_link_time_driver_dependency(boa):
+    out = subprocess.run(["ldd", boa.LIB_PATH], capture_output=True, text=True).stdout
+    assert "libcuda.so" not in out and "libtorch" not in out
+
+
+def test_capacity_bound(boa):
+    for n in (1, 2, 100, 4096, 16384, 1 << 20):
+        w = boa.capacity_words(n)
+        assert w * 32 >= n * 24.01 + 64
+
+
+def test_load_rejects_bad_arguments(boa, weights, tmp_path):
+    with pytest.raises(boa.BoaError) as e:
+        boa.Model(str(tmp_path / "missing.bin"), "mamba", 64, 1)
+    assert e.value.code == boa.BOA_E_IO
+    with pytest.raises(boa.BoaError) as e:
+        boa.Model(weights("mamba", 64, 2, 3), "mamba", 64, 3)  # dims do not match the file
+    assert e.value.code == boa.BOA_E_FORMAT
+    with pytest.raises(boa.BoaError) as e:
+        boa.Model(weights("mamba", 64, 2, 3), "lstm", 64, 2)
+    assert e.value.code == boa.BOA_E_INVALID
+    p = tmp_path / "bad_magic.bin"
+    p.write_bytes(b"BOA\x07" + b"\0" * 64)
+    with pytest.raises(boa.BoaError) as e:
+        boa.Model(str(p), "mamba", 64, 1)
+    assert e.value.code == boa.BOA_E_FORMAT
+
+
+def test_null_handle_is_rejected(boa):
+    L = boa.lib()
+    assert L.boa_set_temperature(None, 1.0) == boa.BOA_E_INVALID
+    assert L.boa_sync(None) == boa.BOA_E_INVALID
+    assert L.boa_device_bytes(None) == 0
+
+
+def _streams(rng, n, chunk):
+    sizes = rng.integers(0, chunk // 4, n).astype(np.uint32)
+    sizes[-1] = 0
+    pay = rng.integers(0, 2**32, int(sizes.sum()), dtype=np.uint64).astype(np.uint32)
+    return sizes, pay
+
+
+@pytest.mark.parametrize("n", [1, 5, 300])
+def test_container_matches_restatement(boa, boa2, n):
+    rng = np.random.default_rng(n)
+    chunk = 1000
+    sizes, pay = _streams(rng, n, chunk)
+    total = (n - 1) * chunk + 7
+    fb = rng.integers(0, 256, n).astype(np.uint8)
+    blob = boa.boa2_build(total, chunk, fb, sizes, pay)
+    streams, o = [], 0
+    for s in sizes:
+        streams.append(pay[o:o + s].tobytes())
+        o += int(s)
+    assert blob == boa2.build(total, chunk, fb, streams)
+    p = boa.boa2_parse(blob)
+    assert p["total_size"] == total and p["n_chunks"] == n and p["last_chunk_len"] == 7
+    assert p["streams"] == streams and np.array_equal(p["first_bytes"], fb)
+
+
+def test_container_parses_reference_files(boa, boa2):
+    for name in ("ref_exact.boa", "ref_rand_d256L8.boa"):
+        blob = open(os.path.join(GOLDEN, name), "rb").read()
+        a, b = boa.boa2_parse(blob), boa2.parse(blob)
+        assert a["streams"] == b["streams"] and list(a["first_bytes"]) == b["first_bytes"]
+        assert boa.boa2_build(a["total_size"], a["chunk_len"], a["first_bytes"],
+                              [len(s) // 4 for s in a["streams"]],
+                              np.frombuffer(b"".join(a["streams"]), "<u4")) == blob
+
+
+def test_container_idx1_accepted(boa, boa2):
+    import struct, zlib
+    blob = open(os.path.join(GOLDEN, "ref_exact.boa"), "rb").read()
+    p = boa2.parse(blob)
+    idx_pos = blob.rfind(b"IDX2")
+    offs, o = [], 0
+    for s in p["streams"]:
+        offs.append(o)
+        o += len(s)
+    idx = b"IDX1" + bytes(p["first_bytes"])
+    prev = 0
+    for x in offs:
+        idx += boa2.uvarint(x - prev)
+        prev = x
+    idx += b"".join(boa2.uvarint(len(s)) for s in p["streams"])
+    v1 = blob[:idx_pos] + idx + struct.pack("<I", zlib.crc32(idx))
+    assert boa.boa2_parse(v1)["streams"] == p["streams"]
+
+
+@pytest.mark.parametrize("damage", ["crc", "magic", "version", "truncate", "range", "no_index"])
+def test_container_rejects_damaged_files(boa, damage):
+    blob = bytearray(open(os.path.join(GOLDEN, "ref_exact.boa"), "rb").read())
+    if damage == "crc":
+        blob[-1] ^= 0x55
+    elif damage == "magic":
+        blob[0:4] = b"BOA3"
+    elif damage == "version":
+        blob[4] = 2
+    elif damage == "truncate":
+        blob = blob[:20]
+    elif damage == "range":
+        # claim a longer first stream, re-CRC so only the range check can catch it
+        import struct, zlib
+        i = blob.rfind(b"IDX2")
+        n = struct.unpack_from("<I", blob, 24)[0]
+        q = i + 4 + n
+        blob[q] = 0xFF
+        blob[q + 1] = 0xFF | 0x80 if False else 0x7F
+        body = bytes(blob[i:-4])
+        blob[-4:] = struct.pack("<I", zlib.crc32(body))
+    elif damage == "no_index":
+        i = blob.rfind(b"IDX2")
+        blob[i:i + 4] = b"XXXX"
+    with pytest.raises(boa.BoaError) as e:
+        boa.boa2_parse(bytes(blob))
+    assert e.value.code == boa.BOA_E_FORMAT

@@ -1,0 +1,203 @@
+"""GPU parity tests: the CUDA path through the C ABI against the CPU oracle
+(pinned to the reference) and the reference's golden outputs."""
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, dirichlet_cdfs
+
+pytestmark = pytest.mark.gpu
+
+# fp32 logits gate (north star): |gpu - oracle| <= 1e-3 * max|oracle| per tensor
+LOGIT_RTOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def m64(boa, weights):
+    return boa.Model(weights("mamba", 64, 2, 3), "mamba", 64, 2)
+
+
+@pytest.fixture(scope="module")
+def m256(boa, weights):
+    return boa.Model(weights("mamba", 256, 8, 0), "mamba", 256, 8)
+
+
+# ---------------------------------------------------------------- coder
+@pytest.mark.parametrize("n_streams,n_steps", [(1, 1), (7, 300), (64, 1000)])
+def test_rc_encode_cdf_bit_exact(boa, oracle, m64, n_streams, n_steps):
+    rng = np.random.default_rng(n_streams * 1000 + n_steps)
+    Q, syms = dirichlet_cdfs(rng, n_steps, n_streams)
+    sizes, pay = m64.rc_encode_cdf(Q, syms)
+    o = 0
+    for s in range(n_streams):
+        ref = oracle.rc_encode_cdf(Q[:, s], syms[:, s])
+        assert sizes[s] == ref.size
+        assert np.array_equal(pay[o:o + sizes[s]], ref)
+        o += int(sizes[s])
+    back = m64.rc_decode_cdf(Q, sizes, pay)
+    assert np.array_equal(back, syms)
+
+
+def test_rc_frequency_one_symbols(boa, oracle, m64):
+    n = 500
+    Q = np.zeros((n, 2, 257), np.uint32)
+    Q[..., :256] = np.arange(256, dtype=np.uint32)
+    Q[..., 1:256] += (1 << 24) - 256
+    Q[..., 256] = 1 << 24
+    syms = np.random.default_rng(3).integers(1, 256, (n, 2)).astype(np.uint8)
+    sizes, pay = m64.rc_encode_cdf(Q, syms)
+    ref = oracle.rc_encode_cdf(Q[:, 0], syms[:, 0])
+    assert np.array_equal(pay[:sizes[0]], ref)
+    assert np.array_equal(m64.rc_decode_cdf(Q, sizes, pay), syms)
+
+
+# ---------------------------------------------------------------- quantiser
+def test_cdf_exact_logits_bit_exact(boa, oracle, m64):
+    rng = np.random.default_rng(5)
+    lg = np.where(rng.random((300, 256)) < 0.3, 0.0, -1000.0).astype(np.float32)
+    lg[:, 7] = 0.0
+    assert np.array_equal(m64.cdf_from_logits(lg), oracle.cdf_rows(lg))
+
+
+def test_cdf_general_logits_close(boa, oracle, m64):
+    rng = np.random.default_rng(6)
+    lg = (rng.standard_normal((500, 256)) * 3).astype(np.float32)
+    q_gpu, q_orc = m64.cdf_from_logits(lg), oracle.cdf_rows(lg)
+    # CUDA __expf vs libm expf: a few units of 2^-24 in the CDF
+    assert np.abs(q_gpu.astype(np.int64) - q_orc.astype(np.int64)).max() <= 64
+    assert np.all(np.diff(q_gpu.astype(np.int64), axis=1) >= 1)
+
+
+# ---------------------------------------------------------------- model logits
+@pytest.mark.parametrize("cfg", ["d64L2", "d256L8"])
+def test_logits_vs_reference_golden(boa, oracle, manifest, weights, cfg):
+    c = next(x for x in manifest["logits"] if x["name"] == cfg)
+    z = np.load(f"{GOLDEN}/ref_logits_{cfg}.npz")
+    m = boa.Model(weights("mamba", c["d_model"], c["n_layers"], c["seed"]), "mamba", c["d_model"], c["n_layers"])
+    for mode in (0, 1):
+        lg = m.logits(z["tokens"], mode)
+        ref = z["chunk"]
+        rel = np.abs(lg - ref).max() / np.abs(ref).max()
+        assert rel <= LOGIT_RTOL, rel
+
+
+def test_logits_vs_oracle_d256L8(boa, oracle, m256, weights):
+    tok = np.random.default_rng(8).integers(0, 256, (3, 130), dtype=np.uint8)
+    om = oracle.OracleModel(weights("mamba", 256, 8, 0), 0, 256, 8)
+    ref = om.logits(tok, 0)
+    lg = m256.logits(tok, 0)
+    rel = np.abs(lg - ref).max() / np.abs(ref).max()
+    assert rel <= LOGIT_RTOL, rel
+
+
+@pytest.mark.parametrize("B,L", [(1, 5), (3, 130), (130, 3)])
+def test_compress_and_decompress_forms_bitwise_equal(boa, m256, B, L):
+    """The decoder regenerates the encoder's CDFs only if the step form
+    (M = chunks) and the tile form (M = chunks x positions) agree bitwise."""
+    tok = np.random.default_rng(B * 31 + L).integers(0, 256, (B, L), dtype=np.uint8)
+    assert np.array_equal(m256.logits(tok, 0), m256.logits(tok, 1))
+
+
+# ---------------------------------------------------------------- codec
+def test_exact_container_matches_reference_binary(boa, manifest, golden_mod, wdir):
+    E = manifest["exact"]
+    p = str(wdir / "exact_gpu.bin")
+    boa.synth.write_weights(p, boa.synth.exact_logit_weights(E["d_model"], E["n_layers"], E["seed"], E["support"]))
+    m = boa.Model(p, "mamba", E["d_model"], E["n_layers"])
+    data = golden_mod.exact_input(E)
+    fb, sizes, pay = m.compress(data, E["chunk"])
+    blob = boa.boa2_build(len(data), E["chunk"], fb, sizes, pay)
+    assert blob == open(f"{GOLDEN}/ref_exact.boa", "rb").read()
+    c = boa.boa2_parse(blob)
+    lens = [E["chunk"]] * (c["n_chunks"] - 1) + [c["last_chunk_len"]]
+    assert m.decompress(fb, sizes, pay, lens, E["chunk"]) == data
+
+
+def _roundtrip(boa, m, data, chunk):
+    fb, sizes, pay = m.compress(data, chunk)
+    n = len(sizes)
+    lens = [chunk] * (n - 1) + [len(data) - (n - 1) * chunk]
+    assert m.decompress(fb, sizes, pay, lens, chunk) == data
+    return fb, sizes, pay
+
+
+def test_roundtrip_and_bits_per_byte_vs_reference(boa, manifest, m256):
+    R = manifest["rand"]
+    data = boa.synth.particle_stream(R["n_bytes"], R["data_seed"])
+    fb, sizes, pay = _roundtrip(boa, m256, data, R["chunk"])
+    blob = boa.boa2_build(len(data), R["chunk"], fb, sizes, pay)
+    bpb = 8.0 * len(blob) / len(data)
+    assert abs(bpb - manifest["rand_result"]["bits_per_byte"]) <= 0.005 * manifest["rand_result"]["bits_per_byte"]
+
+
+@pytest.mark.parametrize("n,chunk,batch,tile", [(1, 64, 0, 0), (2, 64, 0, 0), (1001, 250, 0, 0),
+                                                (1001, 250, 3, 0), (3000, 1000, 2, 7), (4097, 4096, 0, 0)])
+def test_roundtrip_edges(boa, m64, n, chunk, batch, tile):
+    """ragged last chunk (incl. length 1 -> zero-word stream), single chunk,
+    several batches, a tile length that does not divide the chunk."""
+    data = bytes(np.random.default_rng(n + chunk).integers(0, 256, n, dtype=np.uint8))
+    m64.set_batch(batch, tile)
+    try:
+        fb, sizes, pay = _roundtrip(boa, m64, data, chunk)
+    finally:
+        m64.set_batch(0, 0)
+    if n % chunk == 1:
+        assert sizes[-1] == 0
+
+
+def test_tile_size_does_not_change_the_stream(boa, m64):
+    data = bytes(np.random.default_rng(9).integers(0, 256, 3000, dtype=np.uint8))
+    outs = []
+    for tile in (0, 5, 64):
+        m64.set_batch(0, tile)
+        outs.append(m64.compress(data, 1000))
+    m64.set_batch(0, 0)
+    for o in outs[1:]:
+        assert all(np.array_equal(a, b) for a, b in zip(outs[0], o))
+
+
+def test_temperature_roundtrip(boa, m64):
+    data = bytes(np.random.default_rng(10).integers(0, 256, 1500, dtype=np.uint8))
+    m64.set_temperature(0.5)
+    try:
+        _roundtrip(boa, m64, data, 500)
+    finally:
+        m64.set_temperature(1.0)
+
+
+def test_mingru_roundtrip_and_logits(boa, oracle, weights):
+    p = weights("mingru", 256, 2, 2)
+    m = boa.Model(p, "mingru", 256, 2)
+    tok = np.random.default_rng(11).integers(0, 256, (2, 40), dtype=np.uint8)
+    ref = oracle.OracleModel(p, 3, 256, 2).logits(tok, 0)
+    lg = m.logits(tok, 0)
+    assert np.abs(lg - ref).max() <= LOGIT_RTOL * np.abs(ref).max()
+    assert np.array_equal(lg, m.logits(tok, 1))
+    data = boa.synth.particle_stream(5000, 3)
+    _roundtrip(boa, m, data, 1024)
+
+
+def test_cli_roundtrip(boa, weights, tmp_path):
+    data = boa.synth.particle_stream(20000, 5)
+    src, enc, dec = tmp_path / "in.bin", tmp_path / "x.boa", tmp_path / "out.bin"
+    src.write_bytes(data)
+    w = weights("mamba", 64, 2, 3)
+    r = subprocess.run([boa.CLI_PATH, "compress", w, str(src), str(enc), "64", "2", "--chunk-size", "3000"],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([boa.CLI_PATH, "decompress", w, str(enc), str(dec), "64", "2"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    assert dec.read_bytes() == data
+
+
+def test_state_reset_after_a_larger_batch(boa, m64):
+    """A call with fewer chunks than an earlier one must start from zero state
+    in every layer."""
+    big = bytes(np.random.default_rng(12).integers(0, 256, 40 * 300, dtype=np.uint8))
+    small = big[:600]
+    a = m64.compress(small, 300)
+    m64.compress(big, 300)
+    b = m64.compress(small, 300)
+    assert all(np.array_equal(x, y) for x, y in zip(a, b))

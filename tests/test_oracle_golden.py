@@ -1,0 +1,96 @@
+"""The CPU oracle against the reference's own outputs (golden fixtures made by
+tests/golden/make_golden.py from the reference binaries).  CPU only."""
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, dirichlet_cdfs
+
+
+@pytest.mark.parametrize("cfg", ["d64L2", "d256L8"])
+@pytest.mark.parametrize("mode", [0, 1])
+def test_oracle_logits_match_reference_gpu(oracle, boa, manifest, wdir, cfg, mode):
+    c = next(x for x in manifest["logits"] if x["name"] == cfg)
+    z = np.load(f"{GOLDEN}/ref_logits_{cfg}.npz")
+    p = str(wdir / f"g_{cfg}.bin")
+    boa.synth.write_random_weights(p, "mamba", c["d_model"], c["n_layers"], c["seed"])
+    m = oracle.OracleModel(p, 0, c["d_model"], c["n_layers"])
+    lg = m.logits(z["tokens"], mode)
+    ref = z["chunk" if mode == 0 else "step"]
+    # the oracle uses libm exp/log, the reference CUDA's: agree to ~1e-6
+    assert np.abs(lg - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+def test_reference_chunk_and_step_logits_agree(manifest):
+    for c in manifest["logits"]:
+        z = np.load(f"{GOLDEN}/ref_logits_{c['name']}.npz")
+        assert np.array_equal(z["chunk"], z["step"])
+
+
+def test_oracle_reproduces_reference_container_bit_exact(oracle, boa, boa2, manifest, golden_mod, wdir):
+    E = manifest["exact"]
+    p = str(wdir / "exact.bin")
+    boa.synth.write_weights(p, boa.synth.exact_logit_weights(E["d_model"], E["n_layers"], E["seed"], E["support"]))
+    data = golden_mod.exact_input(E)
+    m = oracle.OracleModel(p, 0, E["d_model"], E["n_layers"])
+    fb, streams = m.compress(data, E["chunk"])
+    blob = boa2.build(len(data), E["chunk"], fb, [s.tobytes() for s in streams])
+    ref = open(f"{GOLDEN}/ref_exact.boa", "rb").read()
+    assert blob == ref
+    parsed = boa2.parse(ref)
+    out = m.decompress(parsed["first_bytes"], [np.frombuffer(s, "<u4") for s in parsed["streams"]],
+                       parsed["total_size"], parsed["chunk_len"])
+    assert out == data
+
+
+def test_reference_random_container_parses(boa2, manifest):
+    blob = open(f"{GOLDEN}/ref_rand_d256L8.boa", "rb").read()
+    p = boa2.parse(blob)
+    R = manifest["rand"]
+    assert p["total_size"] == R["n_bytes"] and p["chunk_len"] == R["chunk"]
+    assert p["n_chunks"] == R["n_bytes"] // R["chunk"] and p["index_version"] == 2
+    assert all(len(s) % 4 == 0 for s in p["streams"])
+
+
+def test_oracle_coder_roundtrip_dirichlet(oracle):
+    rng = np.random.default_rng(0)
+    Q, syms = dirichlet_cdfs(rng, 3000, 1)
+    w = oracle.rc_encode_cdf(Q[:, 0], syms[:, 0])
+    assert np.array_equal(oracle.rc_decode_cdf(Q[:, 0], w, 3000), syms[:, 0])
+
+
+def test_oracle_coder_frequency_one_symbols(oracle):
+    # every symbol at frequency 1: longest renormalisation and carry runs
+    Q = np.zeros((400, 257), np.uint32)
+    Q[:, :256] = np.arange(256, dtype=np.uint32)
+    Q[:, 256] = 1 << 24
+    Q[:, 255] = 255
+    Q[:, 1:256] += (1 << 24) - 256  # symbol 0 takes almost everything
+    syms = np.random.default_rng(1).integers(1, 256, 400).astype(np.uint8)
+    w = oracle.rc_encode_cdf(Q, syms)
+    assert np.array_equal(oracle.rc_decode_cdf(Q, w, 400), syms)
+
+
+def test_oracle_empty_stream_is_zero_words(oracle):
+    Q = np.zeros((0, 257), np.uint32)
+    assert oracle.rc_encode_cdf(Q, np.zeros(0, np.uint8)).size == 0
+
+
+def test_oracle_codec_roundtrip_ragged(oracle, weights):
+    m = oracle.OracleModel(weights("mamba", 64, 2, 3), 0, 64, 2)
+    data = bytes(np.random.default_rng(2).integers(0, 256, 2301, dtype=np.uint8))
+    fb, st = m.compress(data, 500)
+    assert [len(s) for s in st][-1] > 0
+    assert m.decompress(fb, st, len(data), 500) == data
+    fb, st = m.compress(data[:2001], 500)  # last chunk of one byte -> zero words
+    assert len(st[-1]) == 0
+    assert m.decompress(fb, st, 2001, 500) == data[:2001]
+
+
+def test_oracle_mingru_roundtrip(oracle, weights):
+    m = oracle.OracleModel(weights("mingru", 64, 2, 2), 3, 64, 2)
+    data = bytes(np.random.default_rng(4).integers(0, 256, 700, dtype=np.uint8))
+    fb, st = m.compress(data, 300)
+    assert m.decompress(fb, st, len(data), 300) == data
+    a = m.logits(np.frombuffer(data[:64], np.uint8).reshape(2, 32), 0)
+    b = m.logits(np.frombuffer(data[:64], np.uint8).reshape(2, 32), 1)
+    assert np.array_equal(a, b)
