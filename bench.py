@@ -1,0 +1,398 @@
+"""Benchmark: BoaConstrictor chunk-parallel compress + decompress on B200.
+
+Workload: the 256-d / 8-layer Mamba predictor,
+random-init weights (seed 0), over a 256 MiB stream of seeded synthetic
+float32 particle records (seed 1 + rank) split into 16,384 chunks of 16 KiB,
+all chunks in one batch.  One step = compress the whole stream on the GPU and
+decompress it again (a byte-exact round trip, verified after timing).
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference]
+
+Under torchrun each rank drives its own GPU with its own 256 MiB shard (weak
+scaling; chunks are independent so no collective touches the data path; the
+only cross-rank traffic is the barrier and the max-reduction of the timings).
+
+value  = MB/s (2^20 B) of input round-tripped per second, whole job, inputs
+         resident in HBM, device time (CUDA events) max over ranks.
+e2e    = the same through the host-buffer C-ABI calls (boa_compress_chunks /
+         boa_decompress_chunks) from pinned host memory, copies included.
+--impl reference times the CPU restatement of the reference path on this
+host's cores (the reference ships no CPU C++ path; its CUDA binary is timed
+separately).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+MiB = float(1 << 20)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--chunks", type=int, default=16384, help="chunks per GPU (configs[2]: 16384)")
+    ap.add_argument("--chunk-len", type=int, default=16384, help="bytes per chunk (configs[2]: 16384)")
+    ap.add_argument("--d-model", type=int, default=256)
+    ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--warmup-chunk-len", type=int, default=256,
+                    help="chunk length of the warm-up steps (same chunks, truncated)")
+    ap.add_argument("--e2e-steps", type=int, default=1)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_info():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# --------------------------------------------------------------------------- roofline
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), float(j["bf16_tflops_sustained"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def algorithmic_per_launch(cls, B, T, d, L):
+    """Algorithmic work of one launch of kernel class `cls` over B chunks x T
+    positions (M = B*T rows): ('hbm', bytes) or ('tensor', flops).  FLOPs
+    count the three bf16 products of the split-precision GEMM."""
+    M, di = B * T, 2 * d
+    xp = ((d + 15) // 16 + 32 + 15) // 16 * 16
+    gem = {"in_proj": (d, 4 * d), "x_proj": (di, xp), "out_proj_ln": (di, d), "ff1_gelu": (d, 4 * d),
+           "ff2_res_ln": (4 * d, d), "head1": (d, d), "head2_coder": (d, 256)}
+    if cls in gem:
+        K, N = gem[cls]
+        return "tensor", 2.0 * 3 * M * N * K
+    if cls == "scan":
+        # state r+w (16 floats/channel) + u, z in + bf16 hi/lo y out (+ delta rows)
+        return "hbm", B * di * 16 * 4 * 2 + M * di * (4 + 4 + 4) + M * xp * 4
+    if cls == "conv":
+        return "hbm", B * di * 3 * 4 * 2 + M * di * (4 + 4 + 4)
+    if cls == "embed_ln":
+        return "hbm", M * (d * 4 + d * 4)
+    if cls == "encode_tile":
+        return "hbm", M * 8 + M * 1
+    return None, 0.0
+
+
+# --------------------------------------------------------------------------- clocks
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.flush()
+        rows = [r.split(",") for r in open(self.f.name).read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        mx = float(rows[0][2])
+        under = [s for s in sm if s > 0.5 * mx] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(under), "sm_max_mhz": mx, "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------- CPU legs
+def cpu_sample(weights, d, L, chunk_len, seed, budget_s, threads):
+    """Round trip of the CPU restatement on `threads` chunks, each a prefix of
+    a configs[2] chunk, sized so one pass takes about budget_s seconds."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.build()
+    boa = __import__("__graft_entry__").load_package()
+    m = O.OracleModel(weights, 0, d, L)
+    data = boa.synth.particle_stream(threads * chunk_len, seed)
+    # calibrate: 64-byte prefixes
+    probe = 64
+    sub = b"".join(data[i * chunk_len: i * chunk_len + probe] for i in range(threads))
+    t = time.perf_counter()
+    fb, st = m.compress(sub, probe, threads=threads)
+    m.decompress(fb, st, len(sub), probe, threads=threads)
+    rate = len(sub) / (time.perf_counter() - t)
+    plen = int(max(probe, min(chunk_len, rate * budget_s / threads)))
+    sub = b"".join(data[i * chunk_len: i * chunk_len + plen] for i in range(threads))
+    t = time.perf_counter()
+    fb, st = m.compress(sub, plen, threads=threads)
+    out = m.decompress(fb, st, len(sub), plen, threads=threads)
+    dt = time.perf_counter() - t
+    assert out == sub
+    return len(sub) / MiB / dt, f"{threads} chunks x {plen}-byte prefixes of configs[2] chunks, round trip", dt
+
+
+def run_reference(a):
+    ws, rank, _ = dist_info()
+    if rank != 0:
+        return
+    sys.path.insert(0, ROOT)
+    boa = __import__("__graft_entry__").load_package()
+    threads = os.cpu_count() or 1
+    with tempfile.TemporaryDirectory() as td:
+        w = os.path.join(td, "w.bin")
+        boa.synth.write_random_weights(w, "mamba", a.d_model, a.layers, 0)
+        for _ in range(a.warmup):
+            cpu_sample(w, a.d_model, a.layers, a.chunk_len, 1, 0.2, threads)
+        vals = []
+        for _ in range(a.steps):
+            v, sample, _ = cpu_sample(w, a.d_model, a.layers, a.chunk_len, 1, a.cpu_seconds, threads)
+            vals.append(v)
+    v = statistics.median(vals)
+    line = {"metric": "compress+decompress round-trip MB/s", "value": v, "unit": "MB/s", "n_gpus": ws,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"configs[2] mamba d{a.d_model} L{a.layers}, chunk {a.chunk_len} B, CPU sample"},
+            "cpu_baseline": {"value": v, "unit": "MB/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "MB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU leg
+def main():
+    a = parse()
+    if a.impl == "reference":
+        return run_reference(a)
+    import torch
+    ws, rank, local = dist_info()
+    dist = None
+    if ws > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    boa = __import__("__graft_entry__").load_package()
+    boa.lib()
+    hbm_peak, tf_burst, tf_sust, peak_kind = load_peaks()
+
+    td = tempfile.mkdtemp()
+    wpath = os.path.join(td, f"w{rank}.bin")
+    boa.synth.write_random_weights(wpath, "mamba", a.d_model, a.layers, 0)
+    m = boa.Model(wpath, "mamba", a.d_model, a.layers, device=local)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    m.set_stream(stream.cuda_stream)
+
+    C, S = a.chunks, a.chunk_len
+    n = C * S
+    host = np.frombuffer(boa.synth.particle_stream(n, 1 + rank), np.uint8)
+    data = torch.from_numpy(host.copy()).to(dev)
+    cap = C * boa.capacity_words(S)
+    payload = torch.empty(cap, dtype=torch.int32, device=dev)
+    sizes = torch.empty(C, dtype=torch.int32, device=dev)
+    offsets = torch.empty(C + 1, dtype=torch.int64, device=dev)
+    first = torch.empty(C, dtype=torch.uint8, device=dev)
+    out = torch.empty(n, dtype=torch.uint8, device=dev)
+
+    def step(chunk_len, nbytes, src=None):
+        src = data if src is None else src
+        m.compress_device(src.data_ptr(), nbytes, chunk_len, C, first.data_ptr(), payload.data_ptr(), cap,
+                          sizes.data_ptr(), offsets.data_ptr())
+        mid = torch.cuda.Event(enable_timing=True)
+        mid.record(stream)
+        m.decompress_device(payload.data_ptr(), offsets.data_ptr(), sizes.data_ptr(), first.data_ptr(), nbytes,
+                            chunk_len, C, out.data_ptr())
+        return mid
+
+    # warm-up: same C chunks, truncated to warmup_chunk_len bytes each
+    wl = min(a.warmup_chunk_len, S)
+    wdata = data.view(C, S)[:, :wl].contiguous().view(-1)
+    for _ in range(a.warmup):
+        step(wl, C * wl, wdata)
+    m.sync()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    clocks = Clocks(local)
+    clocks.start()
+    l0 = m.launch_count()
+    t_comp, t_dec = [], []
+    for _ in range(a.steps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e2 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        mid = step(S, n)
+        e2.record(stream)
+        e2.synchronize()
+        t_comp.append(e0.elapsed_time(mid))
+        t_dec.append(mid.elapsed_time(e2))
+    m.sync()
+    launches = (m.launch_count() - l0) // max(1, a.steps)
+    clk = clocks.stop()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ok = bool(torch.equal(out, data))
+    total_words = int(offsets[C].item())
+    comp_ms = statistics.median(t_comp)
+    dec_ms = statistics.median(t_dec)
+    t = torch.tensor([comp_ms, dec_ms, comp_ms + dec_ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    comp_ms, dec_ms, step_ms = t.tolist()
+    # BOA2 file size of this rank's stream (header 33 B, payload, index, CRC)
+    sz = sizes.cpu().numpy().astype(np.int64) * 4
+    varint = np.ones_like(sz) + (sz >= 1 << 7) + (sz >= 1 << 14) + (sz >= 1 << 21) + (sz >= 1 << 28)
+    boa_bytes = 33 + total_words * 4 + 4 + C + int(varint.sum()) + 4
+    bpb = 8.0 * boa_bytes / n
+
+    # ---- e2e through the host-buffer C ABI (pinned host memory)
+    h_in = torch.from_numpy(host.copy()).pin_memory()
+    h_pay = torch.empty(cap, dtype=torch.int32).pin_memory()
+    h_sizes = np.zeros(C, np.uint32)
+    h_first = np.zeros(C, np.uint8)
+    h_out = torch.empty(n, dtype=torch.uint8).pin_memory()
+    lens = np.full(C, S, np.uint32)
+    import ctypes as Ct
+    L = boa.lib()
+    e2e_ms = []
+    e2e_words = 0
+    for _ in range(a.e2e_steps):
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        used = Ct.c_uint64()
+        rc = L.boa_compress_chunks(m.h, Ct.cast(h_in.data_ptr(), boa._u8p), n, S, 0, C,
+                                   h_first.ctypes.data_as(boa._u8p), Ct.cast(h_pay.data_ptr(), boa._u32p), cap,
+                                   h_sizes.ctypes.data_as(boa._u32p), Ct.byref(used))
+        boa._check(rc, m.h)
+        rc = L.boa_decompress_chunks(m.h, Ct.cast(h_pay.data_ptr(), boa._u32p), h_sizes.ctypes.data_as(boa._u32p),
+                                     h_first.ctypes.data_as(boa._u8p), lens.ctypes.data_as(boa._u32p), S, C,
+                                     Ct.cast(h_out.data_ptr(), boa._u8p))
+        boa._check(rc, m.h)
+        s1.record(stream)
+        s1.synchronize()
+        e2e_ms.append(s0.elapsed_time(s1))
+        e2e_words = used.value
+    e2e_ok = bool(torch.equal(h_out, h_in)) if a.e2e_steps > 0 else True
+    te = torch.tensor([statistics.median(e2e_ms) if e2e_ms else float("nan")], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_step_ms = te.item()
+
+    # ---- per-kernel timing: instrumented pass (events around every launch)
+    # over one compress tile and 8 decode steps of the same C chunks
+    m.set_profiling(True)
+    m.profile()
+    T = 64
+    tl = T + 1
+    tdata = data.view(C, S)[:, :tl].contiguous().view(-1)
+    m.compress_device(tdata.data_ptr(), C * tl, tl, C, first.data_ptr(), payload.data_ptr(), cap,
+                      sizes.data_ptr(), offsets.data_ptr())
+    prof_c = m.profile()
+    m.decompress_device(payload.data_ptr(), offsets.data_ptr(), sizes.data_ptr(), first.data_ptr(), C * 9, 9, C,
+                        out.data_ptr())
+    prof_d = m.profile()
+    m.set_profiling(False)
+    kern = {}
+    steps_c = -(-(S - 1) // T)  # compress tiles per step
+    steps_d = S - 1             # decode steps per step
+    for name in prof_c:
+        cms, cn = prof_c[name]
+        dms, dn = prof_d[name]
+        kern[name] = {"compress_ms_per_launch": cms / cn if cn else 0.0, "compress_launches": cn,
+                      "decode_ms_per_launch": dms / dn if dn else 0.0, "decode_launches": dn,
+                      "est_ms_per_step": (cms * steps_c + dms / 8 * steps_d)}
+    dom = max(kern, key=lambda k: kern[k]["est_ms_per_step"])
+    kd = kern[dom]
+    in_decode = kd["decode_ms_per_launch"] * kd["decode_launches"] / 8 * steps_d >= kd["compress_ms_per_launch"] * kd["compress_launches"] * steps_c
+    if in_decode:
+        bound, work = algorithmic_per_launch(dom, C, 1, a.d_model, a.layers)
+        dur = kd["decode_ms_per_launch"]
+        phase = "decompress step (M = 16384 chunks)"
+    else:
+        bound, work = algorithmic_per_launch(dom, C, T, a.d_model, a.layers)
+        dur = kd["compress_ms_per_launch"]
+        phase = f"compress tile (M = {C} x {T})"
+    if bound == "tensor":
+        achieved = work / (dur * 1e-3) / 1e12
+        peak, unit = tf_sust, "TFLOP/s"
+    else:
+        achieved = work / (dur * 1e-3) / 1e9
+        peak, unit = hbm_peak, "GB/s"
+
+    # ---- CPU baseline (rank 0, N = 1 only)
+    cpu = None
+    if rank == 0 and ws == 1 and not a.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        v, sample, _ = cpu_sample(wpath, a.d_model, a.layers, S, 1, a.cpu_seconds, threads)
+        cpu = {"value": v, "unit": "MB/s", "cores": threads, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        total = n * ws
+        line = {
+            "metric": "compress+decompress round-trip MB/s",
+            "value": total / MiB / (step_ms * 1e-3),
+            "unit": "MB/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup, "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16x3 (fp32-accurate)",
+            "data": "synthetic: seeded float32 particle records, random-init weights",
+            "config": {"workload": "configs[2]: mamba d256 L8, 16384 chunks x 16 KiB = 256 MiB per GPU, one batch",
+                       "d_model": a.d_model, "n_layers": a.layers, "chunks_per_gpu": C, "chunk_len": S,
+                       "batch_chunks": C, "compress_tile": T, "parallelism": f"chunk-sharded x{ws}",
+                       "l2": "inputs (256 MiB) and recurrent state (5 GiB) exceed L2; no flush needed",
+                       "warmup": f"{a.warmup} round trips of the same chunks truncated to {wl} B"},
+            "compress_MBps": total / MiB / (comp_ms * 1e-3),
+            "decompress_MBps": total / MiB / (dec_ms * 1e-3),
+            "bits_per_byte": bpb, "roundtrip_ok": ok and e2e_ok,
+            "roofline": {"kernel": dom, "phase": phase, "bound": bound, "achieved": achieved, "peak": peak,
+                         "unit": unit, "frac": achieved / peak, "traffic": None,
+                         "peak_source": f"{peak_kind} ({'bf16 sustained' if bound == 'tensor' else 'HBM copy'})"},
+            "kernels": kern,
+            "cpu_baseline": cpu,
+            "e2e": {"value": total / MiB / (e2e_step_ms * 1e-3), "unit": "MB/s",
+                    "h2d_bytes_per_step": n + e2e_words * 4 + C * 9,
+                    "d2h_bytes_per_step": e2e_words * 4 + C * 5 + 8 + n},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

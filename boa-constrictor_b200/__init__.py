@@ -29,6 +29,7 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "boa_b200.h")
 
 BOA_OK, BOA_E_INVALID, BOA_E_CUDA, BOA_E_IO, BOA_E_FORMAT, BOA_E_DEVICE, BOA_E_NOMEM = 0, -1, -2, -3, -4, -5, -6
 BACKBONES = {"mamba": 0, "mambav1": 0, "mingru": 3}
+PROF_CLASSES = 12
 
 _u8p, _u32p, _u64p, _f32p = (C.POINTER(C.c_uint8), C.POINTER(C.c_uint32), C.POINTER(C.c_uint64),
                              C.POINTER(C.c_float))
@@ -72,6 +73,10 @@ SIGNATURES = {
                                         C.c_uint32, C.c_uint32, C.c_void_p]),
     "boa_sync": (C.c_int, [C.c_void_p]),
     "boa_device_bytes": (C.c_uint64, [C.c_void_p]),
+    "boa_set_profiling": (C.c_int, [C.c_void_p, C.c_int]),
+    "boa_profile_read": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_double), _u64p]),
+    "boa_profile_name": (C.c_char_p, [C.c_int]),
+    "boa_launch_count": (C.c_uint64, [C.c_void_p]),
     "boa_model_logits": (C.c_int, [C.c_void_p, _u8p, C.c_int, C.c_int, C.c_int, _f32p]),
     "boa_rc_encode_cdf": (C.c_int, [C.c_void_p, _u32p, _u8p, C.c_int, C.c_int, _u32p, C.c_size_t, _u32p]),
     "boa_rc_decode_cdf": (C.c_int, [C.c_void_p, _u32p, C.c_int, C.c_int, _u32p, _u32p, _u8p]),
@@ -149,6 +154,32 @@ class Model:
 
     def device_bytes(self) -> int:
         return int(lib().boa_device_bytes(self.h))
+
+    def set_profiling(self, on: bool):
+        _check(lib().boa_set_profiling(self.h, int(bool(on))), self.h)
+
+    def profile(self) -> dict:
+        """{kernel class: (total ms, launches)} since the last read."""
+        out = {}
+        for c in range(PROF_CLASSES):
+            ms, n = C.c_double(), C.c_uint64()
+            _check(lib().boa_profile_read(self.h, c, C.byref(ms), C.byref(n)), self.h)
+            out[lib().boa_profile_name(c).decode()] = (ms.value, n.value)
+        return out
+
+    def launch_count(self) -> int:
+        return int(lib().boa_launch_count(self.h))
+
+    # device-buffer API (ints are raw device pointers)
+    def compress_device(self, d_data: int, n_bytes: int, chunk_len: int, n_chunks: int, d_first: int,
+                        d_payload: int, cap_words: int, d_sizes: int, d_offsets: int):
+        _check(lib().boa_compress_device(self.h, d_data, n_bytes, chunk_len, n_chunks, d_first, d_payload,
+                                         cap_words, d_sizes, d_offsets), self.h)
+
+    def decompress_device(self, d_payload: int, d_offsets: int, d_sizes: int, d_first: int, n_bytes: int,
+                          chunk_len: int, n_chunks: int, d_out: int):
+        _check(lib().boa_decompress_device(self.h, d_payload, d_offsets, d_sizes, d_first, n_bytes, chunk_len,
+                                           n_chunks, d_out), self.h)
 
     # ---------------------------------------------------------------- codec
     def compress(self, data: bytes, chunk_len: int, first_chunk: int = 0, n_chunks: int | None = None):

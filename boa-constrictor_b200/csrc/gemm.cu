@@ -18,6 +18,7 @@
 // logits and therefore identical CDFs.
 #include <cuda.h>
 #include <cstdio>
+#include <algorithm>
 #include <mutex>
 #include "gemm.cuh"
 
@@ -287,6 +288,227 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   }
 }
 
+// ------------------------------------------------------------------ persistent
+// Persistent form for the row-parallel epilogues (F32, ACT_SPLIT, LN_SPLIT,
+// RES_LN): one CTA per SM walks tiles t = blockIdx.x, +gridDim.x, ...; two
+// TMEM accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
+//   warp 0      TMA producer (continuous across tiles)
+//   warp 1      TMEM allocator + MMA issuer
+//   warps 2..9  epilogue; warp w reads TMEM lane quarter w % 4 and column
+//               half (w - 2) / 4.  LayerNorm moments are combined across the
+//               two halves in a fixed order (half 0 + half 1).
+constexpr int kPThreads = 320;
+constexpr int kEpiThreads = 256;
+
+template <int BN>
+struct PCfg {
+  static constexpr int kStages = BN >= 256 ? 2 : (BN >= 128 ? 3 : 4);
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;
+  static constexpr int kAccCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr int kTmemCols = 2 * kAccCols;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256 + kBM * 2 * 2 * 4;
+};
+
+template <int BN, int MODE>
+__global__ void __launch_bounds__(kPThreads, 1)
+gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, GemmArgs args) {
+  using Cfg = PCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + Cfg::kStages;
+  uint64_t* acc_full = bars + 2 * Cfg::kStages;       // [2]
+  uint64_t* acc_empty = bars + 2 * Cfg::kStages + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * Cfg::kStages + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red = reinterpret_cast<float*>(smem + Cfg::kStages * Cfg::kStageBytes + 256);  // [128][2 halves][2]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles_n = args.N / BN;
+  const int n_tiles = n_tiles_n * ((args.M + kBM - 1) / kBM);
+  const int nkb = (args.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&acc_full[a], 1); mbar_init(&acc_empty[a], kEpiThreads / 32); }
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmW);
+  }
+  if (warp == 1) { tmem_alloc(tmem_slot, Cfg::kTmemCols); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;  // global k-block counter (stage / phase)
+      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
+        const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          const int s = g % Cfg::kStages;
+          if (g >= Cfg::kStages && !mbar_wait(&empty[s], ((g / Cfg::kStages) - 1) & 1)) { *abort_flag = 1; break; }
+          uint8_t* st = smem + s * Cfg::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+          const int k0 = kb * kBK;
+          tma_load_3d(st, &tmA, &full[s], k0, m0, 0);
+          tma_load_3d(st + Cfg::kABytes, &tmA, &full[s], k0, m0, 1);
+          tma_load_3d(st + 2 * Cfg::kABytes, &tmW, &full[s], k0, n0, 0);
+          tma_load_3d(st + 2 * Cfg::kABytes + Cfg::kBBytes, &tmW, &full[s], k0, n0, 1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
+      int g = 0, it = 0;
+      for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
+        const int a = it & 1;
+        const uint32_t acc = tmem + (uint32_t)(a * Cfg::kAccCols);
+        if (it >= 2 && !mbar_wait(&acc_empty[a], ((it >> 1) - 1) & 1)) { *abort_flag = 1; }
+        if (*abort_flag) { umma_commit(&acc_full[a]); break; }
+        tc_fence_after();
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          const int s = g % Cfg::kStages;
+          if (!mbar_wait(&full[s], (g / Cfg::kStages) & 1)) { *abort_flag = 1; break; }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + s * Cfg::kStageBytes);
+          const uint64_t dAh = umma_desc_sw128(st);
+          const uint64_t dAl = umma_desc_sw128(st + Cfg::kABytes);
+          const uint64_t dWh = umma_desc_sw128(st + 2 * Cfg::kABytes);
+          const uint64_t dWl = umma_desc_sw128(st + 2 * Cfg::kABytes + Cfg::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t adv = (uint64_t)(kk * 32 >> 4);
+            umma_bf16(acc, dAh + adv, dWh + adv, idesc, (kb | kk) != 0);
+            umma_bf16(acc, dAh + adv, dWl + adv, idesc, 1u);
+            umma_bf16(acc, dAl + adv, dWh + adv, idesc, 1u);
+          }
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&acc_full[a]);
+        if (*abort_flag) break;
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r_local = q * 32 + lane;
+    // column range of this half in whole 16-column chunks (BN = 48 -> 32 + 16)
+    constexpr int kChunks = BN / 16;
+    constexpr int kChunks0 = (kChunks + 1) / 2;
+    int it = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
+      const int a = it & 1;
+      const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
+      // only the barrier outcome decides (uniform across the epilogue warps,
+      // which then meet at named barriers)
+      const bool ok = mbar_wait(&acc_full[a], (it >> 1) & 1);
+      tc_fence_after();
+      if (!ok) break;
+      const uint32_t trow = tmem + (uint32_t)(a * Cfg::kAccCols) + ((uint32_t)(q * 32) << 16);
+      const int row = m0 + r_local;
+      const bool live = row < args.M;
+      const int c0 = half ? kChunks0 * 16 : 0;
+      const int c1 = half ? BN : kChunks0 * 16;
+      if constexpr (MODE == EPI_F32) {
+#pragma unroll 1
+        for (int c = c0; c < c1; c += 16) {
+          float v[16];
+          tmem_ld16(trow + c, v);
+          if (args.bias) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += args.bias[n0 + c + j];
+          }
+          if (live) store_f32x16(args.out_f32 + (size_t)row * args.ld_f32 + n0 + c, v);
+        }
+      } else if constexpr (MODE == EPI_ACT_SPLIT) {
+#pragma unroll 1
+        for (int c = c0; c < c1; c += 16) {
+          float v[16];
+          tmem_ld16(trow + c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = apply_act(v[j] + args.bias[n0 + c + j], args.act);
+          if (live) {
+            __nv_bfloat16* hi = args.out_hl + (size_t)row * args.ld_hl + n0 + c;
+            store_split16(hi, hi + args.plane_hl, v);
+          }
+        }
+      } else {  // EPI_LN_SPLIT / EPI_RES_LN: BN == N, full row in this tile
+        float sum = 0.f, sq = 0.f;
+#pragma unroll 1
+        for (int c = c0; c < c1; c += 16) {
+          float v[16];
+          tmem_ld16(trow + c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float x = v[j] + args.bias[c + j];
+            if constexpr (MODE == EPI_RES_LN) x = x + (live ? args.res[(size_t)row * BN + c + j] : 0.f);
+            v[j] = x;
+            sum += x;
+            sq += x * x;
+          }
+          if constexpr (MODE == EPI_RES_LN) {
+            if (live) store_f32x16(args.res + (size_t)row * BN + c, v);
+          }
+        }
+        red[(r_local * 2 + half) * 2 + 0] = sum;
+        red[(r_local * 2 + half) * 2 + 1] = sq;
+        named_bar_sync(1, kEpiThreads);
+        sum = red[(r_local * 2 + 0) * 2 + 0] + red[(r_local * 2 + 1) * 2 + 0];
+        sq = red[(r_local * 2 + 0) * 2 + 1] + red[(r_local * 2 + 1) * 2 + 1];
+        const bool norm = args.ln_w != nullptr;
+        const float mean = sum / (float)BN;
+        const float var = sq / (float)BN - mean * mean;
+        const float inv_std = rsqrtf(var + 1e-5f);
+#pragma unroll 1
+        for (int c = c0; c < c1; c += 16) {
+          float v[16];
+          if constexpr (MODE == EPI_RES_LN) {
+            if (live) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                float4 tt = reinterpret_cast<const float4*>(args.res + (size_t)row * BN + c)[j / 4];
+                v[j] = tt.x; v[j + 1] = tt.y; v[j + 2] = tt.z; v[j + 3] = tt.w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = 0.f;
+            }
+          } else {
+            tmem_ld16(trow + c, v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = v[j] + args.bias[c + j];
+          }
+          if (norm) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = (v[j] - mean) * inv_std * args.ln_w[c + j] + args.ln_b[c + j];
+          }
+          if (live) {
+            __nv_bfloat16* hi = args.out_hl + (size_t)row * args.ld_hl + c;
+            store_split16(hi, hi + args.plane_hl, v);
+          }
+        }
+        named_bar_sync(1, kEpiThreads);  // red[] reused by the next tile
+      }
+      // accumulator a may be overwritten once every epilogue warp has read it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -319,17 +541,31 @@ static bool make_plane_map(CUtensorMap* map, const void* base, int K, int rows, 
   return r == CUDA_SUCCESS;
 }
 
+static int g_num_sms[64] = {0};
+
 template <int BN, int MODE>
 static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tw, const GemmArgs& a, cudaStream_t st) {
-  using Cfg = GemmCfg<BN>;
-  dim3 grid(a.N / BN, (a.M + kBM - 1) / kBM);
-  gemm_kernel<BN, MODE><<<grid, kThreads, Cfg::kSmem, st>>>(ta, tw, a);
+  if constexpr (MODE <= EPI_RES_LN) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int tiles = (a.N / BN) * ((a.M + kBM - 1) / kBM);
+    const int grid = std::min(tiles, g_num_sms[dev & 63] > 0 ? g_num_sms[dev & 63] : 148);
+    gemm_persist_kernel<BN, MODE><<<grid, kPThreads, PCfg<BN>::kSmem, st>>>(ta, tw, a);
+  } else {
+    using Cfg = GemmCfg<BN>;
+    dim3 grid(a.N / BN, (a.M + kBM - 1) / kBM);
+    gemm_kernel<BN, MODE><<<grid, kThreads, Cfg::kSmem, st>>>(ta, tw, a);
+  }
   return cudaGetLastError();
 }
 
 template <int BN, int MODE>
 static cudaError_t set_attr_t() {
-  return cudaFuncSetAttribute(gemm_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::kSmem);
+  if constexpr (MODE <= EPI_RES_LN)
+    return cudaFuncSetAttribute(gemm_persist_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                PCfg<BN>::kSmem);
+  else
+    return cudaFuncSetAttribute(gemm_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::kSmem);
 }
 
 template <int BN>
@@ -368,6 +604,9 @@ static cudaError_t set_attrs() {
 cudaError_t gemm_prepare_device() {
   if (!get_encode_fn()) return cudaErrorNotSupported;
   cudaError_t e;
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&g_num_sms[dev & 63], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
   if ((e = set_attrs<48>()) != cudaSuccess) return e;
   if ((e = set_attrs<64>()) != cudaSuccess) return e;
   if ((e = set_attrs<128>()) != cudaSuccess) return e;

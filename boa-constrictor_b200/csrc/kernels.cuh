@@ -34,6 +34,8 @@ cudaError_t launch_scan(const float* delta, int ld_delta, int r, const float* dt
                         const float* negA, const float* Dv, const float* u, const float* xz, int di,
                         float* ssm_state, __nv_bfloat16* yhl, long long plane, int B, int T, cudaStream_t st);
 
+cudaError_t scan_prepare_device();
+
 // minGRU recurrence: h = (1-z) h + z g(ht) over T rows per chunk; writes h
 // into x_out rows (boa_gpu.hpp:652-693).  zh = [M][2d] (z logits | h~ raw).
 cudaError_t launch_mingru(const float* zh, int d, float* h_state, float* x_out, int B, int T, cudaStream_t st);

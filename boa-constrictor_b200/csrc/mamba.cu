@@ -3,6 +3,7 @@
 // Row layout: rows are (chunk b, position tau) with T rows per chunk; the
 // decompress step is the T = 1 case of the same kernels, so both directions
 // run identical arithmetic per row.
+#include <algorithm>
 #include "kernels.cuh"
 
 namespace boa {
@@ -83,7 +84,9 @@ cudaError_t launch_embed_ln(const TokenSrc& src, const float* emb, int d, float*
 
 // ---------------------------------------------------------------- causal conv
 // Thread per (chunk, channel); window = three carried inputs + current.
-// Sum order bias, oldest tap .. newest (mamba_kernels.cu:158-197, :370-412).
+// Sum order bias, oldest tap .. newest (mamba_kernels.cu:158-197, :370-412),
+// explicit round-to-nearest operations so every launch shape computes the
+// same bits.
 __global__ void conv_kernel(const float* __restrict__ xz, int di, float* __restrict__ cst,
                             const float* __restrict__ cw, const float* __restrict__ cb, float* __restrict__ u,
                             __nv_bfloat16* __restrict__ uhl, long long plane, int B, int T) {
@@ -94,15 +97,17 @@ __global__ void conv_kernel(const float* __restrict__ xz, int di, float* __restr
   float w0 = s[0], w1 = s[di], w2 = s[2 * di];
   const float4 k = reinterpret_cast<const float4*>(cw)[c];
   const float bias = cb[c];
+  float xt_next = xz[(size_t)b * T * 2 * di + c];
   for (int tau = 0; tau < T; ++tau) {
     const size_t row = (size_t)b * T + tau;
-    const float xt = xz[row * 2 * di + c];
+    const float xt = xt_next;
+    if (tau + 1 < T) xt_next = xz[(row + 1) * 2 * di + c];
     float v = bias;
-    v = v + w0 * k.x;
-    v = v + w1 * k.y;
-    v = v + w2 * k.z;
-    v = v + xt * k.w;
-    const float o = v / (1.0f + expf(-v));
+    v = __fadd_rn(v, __fmul_rn(w0, k.x));
+    v = __fadd_rn(v, __fmul_rn(w1, k.y));
+    v = __fadd_rn(v, __fmul_rn(w2, k.z));
+    v = __fadd_rn(v, __fmul_rn(xt, k.w));
+    const float o = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
     u[row * di + c] = o;
     __nv_bfloat16 h, l;
     split_bf16(o, h, l);
@@ -121,20 +126,46 @@ cudaError_t launch_conv(const float* xz, int di, float* cst, const float* cw, co
 }
 
 // ---------------------------------------------------------------- selective scan
-// Thread per (chunk, channel), state h[16] in registers across the T rows.
-// dt = softplus(delta[:r] . Wdt[c] + b) restates dt_proj + softplus
-// (inference_kernels.cu:372-390); the recurrence restates
-// mamba_kernels.cu:271-361 / :414-470; the gate mamba_kernels.cu:130-151.
+// One (row, channel) update of the selective scan, shared by the tile and the
+// step kernels so both compute identical bits:
+//   dt = softplus(delta[:R] . Wdt[c] + b)          (dt_proj, inference_kernels.cu:372-390)
+//   h_n = exp(A_n dt) h_n + dt B_n u ;  y = sum_n h_n C_n + D u   (mamba_kernels.cu:271-361)
+//   out = y * silu(z)                               (mamba_kernels.cu:130-151)
 template <int R>
-__global__ void __launch_bounds__(128) scan_kernel(const float* __restrict__ delta, int ld, const float* __restrict__ dtw,
-                                                   const float* __restrict__ dtb, const float* __restrict__ negA,
-                                                   const float* __restrict__ Dv, const float* __restrict__ u,
-                                                   const float* __restrict__ xz, int di, float* __restrict__ hs,
-                                                   __nv_bfloat16* __restrict__ yhl, long long plane, int T) {
+__device__ __forceinline__ float scan_update(const float* __restrict__ dl, const float (&wdt)[R], float bdt,
+                                             const float (&na)[16], float (&h)[16], float uv, float z, float dsk) {
+  float acc = 0.f;
+#pragma unroll
+  for (int k = 0; k < R; ++k) acc = __fmaf_rn(dl[k], wdt[k], acc);
+  const float dt = logf(__fadd_rn(1.0f, expf(__fadd_rn(acc, bdt))));
+  float y = 0.f;
+#pragma unroll
+  for (int n = 0; n < 16; ++n) {
+    const float dA = __expf(__fmul_rn(na[n], dt));
+    const float dBu = __fmul_rn(__fmul_rn(dt, dl[R + n]), uv);
+    h[n] = __fmaf_rn(dA, h[n], dBu);
+    y = __fmaf_rn(h[n], dl[R + 16 + n], y);
+  }
+  y = __fmaf_rn(uv, dsk, y);
+  return __fmul_rn(y, __fdiv_rn(z, __fadd_rn(1.0f, expf(-z))));
+}
+
+// Compress form: thread per (chunk, channel), h[16] in registers across the T
+// rows of the tile; the chunk's delta rows are staged in shared memory.
+template <int R>
+__global__ void __launch_bounds__(128) scan_tile_kernel(const float* __restrict__ delta, int ld, const float* __restrict__ dtw,
+                                                        const float* __restrict__ dtb, const float* __restrict__ negA,
+                                                        const float* __restrict__ Dv, const float* __restrict__ u,
+                                                        const float* __restrict__ xz, int di, float* __restrict__ hs,
+                                                        __nv_bfloat16* __restrict__ yhl, long long plane, int T) {
   extern __shared__ float sdelta[];  // [T][ld]
   const int b = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  for (int i = threadIdx.x; i < T * ld; i += blockDim.x) sdelta[i] = delta[(size_t)b * T * ld + i];
+  {
+    const float4* src = reinterpret_cast<const float4*>(delta + (size_t)b * T * ld);
+    float4* dst = reinterpret_cast<float4*>(sdelta);
+    for (int i = threadIdx.x; i < T * ld / 4; i += blockDim.x) dst[i] = src[i];
+  }
   __syncthreads();
   if (c >= di) return;
   float wdt[R];
@@ -145,25 +176,12 @@ __global__ void __launch_bounds__(128) scan_kernel(const float* __restrict__ del
 #pragma unroll
   for (int n = 0; n < 16; ++n) { na[n] = negA[(size_t)c * 16 + n]; h[n] = hp[(size_t)n * di]; }
   const float bdt = dtb[c], dsk = Dv[c];
-  for (int tau = 0; tau < T; ++tau) {
-    const float* dl = sdelta + tau * ld;
-    const size_t row = (size_t)b * T + tau;
-    float acc = 0.f;
-#pragma unroll
-    for (int k = 0; k < R; ++k) acc = fmaf(dl[k], wdt[k], acc);
-    const float dt = logf(1.0f + expf(acc + bdt));
-    const float uv = u[row * di + c];
-    float y = 0.f;
-#pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      const float dA = __expf(na[n] * dt);
-      const float dB = dt * dl[R + n];
-      h[n] = dA * h[n] + dB * uv;
-      y = y + h[n] * dl[R + 16 + n];
-    }
-    y = y + uv * dsk;
-    const float z = xz[row * 2 * di + di + c];
-    const float o = y * (z / (1.0f + expf(-z)));
+  size_t row = (size_t)b * T;
+  float un = u[row * di + c], zn = xz[row * 2 * di + di + c];
+  for (int tau = 0; tau < T; ++tau, ++row) {
+    const float uv = un, z = zn;
+    if (tau + 1 < T) { un = u[(row + 1) * di + c]; zn = xz[(row + 1) * 2 * di + di + c]; }
+    const float o = scan_update<R>(sdelta + tau * ld, wdt, bdt, na, h, uv, z, dsk);
     __nv_bfloat16 hh, ll;
     split_bf16(o, hh, ll);
     yhl[row * di + c] = hh;
@@ -173,17 +191,120 @@ __global__ void __launch_bounds__(128) scan_kernel(const float* __restrict__ del
   for (int n = 0; n < 16; ++n) hp[(size_t)n * di] = h[n];
 }
 
+// Decompress form (T = 1): persistent CTAs stream each chunk's 16 x di state
+// (32 KB at di = 512) through shared memory with bulk async copies, three
+// chunks in flight per CTA, so the kernel runs at HBM rate instead of being
+// bound by per-thread load latency.  One thread per channel.
+constexpr int kScanStages = 3;
+template <int R>
+__global__ void __launch_bounds__(1024) scan_step_kernel(const float* __restrict__ delta, int ld,
+                                                         const float* __restrict__ dtw, const float* __restrict__ dtb,
+                                                         const float* __restrict__ negA, const float* __restrict__ Dv,
+                                                         const float* __restrict__ u, const float* __restrict__ xz,
+                                                         int di, float* __restrict__ hs,
+                                                         __nv_bfloat16* __restrict__ yhl, long long plane, int B) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  const uint32_t st_bytes = 16u * di * 4, uz_bytes = (uint32_t)di * 4, dl_bytes = ((uint32_t)ld * 4 + 15) & ~15u;
+  const uint32_t stage_bytes = st_bytes + 2 * uz_bytes + dl_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kScanStages * stage_bytes);
+  const int c = threadIdx.x;
+  if (c == 0) {
+    for (int s = 0; s < kScanStages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int i, int s) {
+    const int b = blockIdx.x + i * gridDim.x;
+    uint8_t* p = sm + s * stage_bytes;
+    mbar_arrive_expect_tx(&full[s], st_bytes + 2 * uz_bytes + (uint32_t)ld * 4);
+    bulk_load(p, hs + (size_t)b * 16 * di, st_bytes, &full[s]);
+    bulk_load(p + st_bytes, u + (size_t)b * di, uz_bytes, &full[s]);
+    bulk_load(p + st_bytes + uz_bytes, xz + (size_t)b * 2 * di + di, uz_bytes, &full[s]);
+    bulk_load(p + st_bytes + 2 * uz_bytes, delta + (size_t)b * ld, (uint32_t)ld * 4, &full[s]);
+  };
+  const int n_mine = (B - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  if (c == 0)
+    for (int s = 0; s < kScanStages && s < n_mine; ++s) issue(s, s);
+  float wdt[R], na[16];
+  float bdt = 0.f, dsk = 0.f;
+  if (c < di) {
+#pragma unroll
+    for (int k = 0; k < R; ++k) wdt[k] = dtw[(size_t)c * R + k];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) na[n] = negA[(size_t)c * 16 + n];
+    bdt = dtb[c];
+    dsk = Dv[c];
+  }
+  bool alive = true;
+  for (int i = 0; i < n_mine; ++i) {
+    const int s = i % kScanStages;
+    const int b = blockIdx.x + i * gridDim.x;
+    uint8_t* p = sm + s * stage_bytes;
+    if (!mbar_wait(&full[s], (i / kScanStages) & 1)) alive = false;
+    if (alive && c < di) {
+      float* hsm = reinterpret_cast<float*>(p);
+      const float* usm = reinterpret_cast<const float*>(p + st_bytes);
+      const float* zsm = usm + di;
+      const float* dl = reinterpret_cast<const float*>(p + st_bytes + 2 * uz_bytes);
+      float h[16];
+#pragma unroll
+      for (int n = 0; n < 16; ++n) h[n] = hsm[n * di + c];
+      const float o = scan_update<R>(dl, wdt, bdt, na, h, usm[c], zsm[c], dsk);
+#pragma unroll
+      for (int n = 0; n < 16; ++n) hsm[n * di + c] = h[n];
+      __nv_bfloat16 hh, ll;
+      split_bf16(o, hh, ll);
+      yhl[(size_t)b * di + c] = hh;
+      yhl[plane + (size_t)b * di + c] = ll;
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (c == 0) {
+      if (alive) {
+        bulk_store(hs + (size_t)b * 16 * di, p, st_bytes);
+        bulk_commit();
+      }
+      if (i + kScanStages < n_mine && alive) {
+        bulk_wait_read_all();  // the store must have read the stage before it is refilled
+        issue(i + kScanStages, s);
+      }
+    }
+  }
+  if (c == 0) bulk_wait_all();
+}
+
 cudaError_t launch_scan(const float* delta, int ld, int r, const float* dtw, const float* dtb, const float* negA,
                         const float* Dv, const float* u, const float* xz, int di, float* hs, __nv_bfloat16* yhl,
                         long long plane, int B, int T, cudaStream_t st) {
+  if (T == 1 && di <= 1024 && (ld * 4) % 16 == 0) {
+    const size_t stage = (size_t)16 * di * 4 + 2 * (size_t)di * 4 + (((size_t)ld * 4 + 15) & ~size_t(15));
+    const size_t sm = kScanStages * stage + kScanStages * 8;
+    int dev = 0, n_sm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    const int per_sm = (int)std::max<size_t>(1, (size_t)(220 * 1024) / sm);
+    const int grid = std::min(B, n_sm * per_sm);
+    switch (r) {
+#define BOA_STEP_CASE(RR)                                                                                          \
+  case RR:                                                                                                         \
+    scan_step_kernel<RR><<<grid, di, sm, st>>>(delta, ld, dtw, dtb, negA, Dv, u, xz, di, hs, yhl, plane, B);       \
+    break;
+      BOA_STEP_CASE(4)
+      BOA_STEP_CASE(8)
+      BOA_STEP_CASE(16)
+      BOA_STEP_CASE(32)
+#undef BOA_STEP_CASE
+      default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+  }
   dim3 block(128), grid((di + 127) / 128, B);
   const size_t sm = (size_t)T * ld * sizeof(float);
-  if (sm > 200 * 1024) return cudaErrorInvalidValue;
+  if (sm > 200 * 1024 || (T * ld) % 4) return cudaErrorInvalidValue;
   switch (r) {
-#define BOA_SCAN_CASE(RR)                                                                                     \
-  case RR:                                                                                                    \
-    if (sm > 48 * 1024) cudaFuncSetAttribute(scan_kernel<RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm); \
-    scan_kernel<RR><<<grid, block, sm, st>>>(delta, ld, dtw, dtb, negA, Dv, u, xz, di, hs, yhl, plane, T);     \
+#define BOA_SCAN_CASE(RR)                                                                                                \
+  case RR:                                                                                                               \
+    scan_tile_kernel<RR><<<grid, block, sm, st>>>(delta, ld, dtw, dtb, negA, Dv, u, xz, di, hs, yhl, plane, T);         \
     break;
     BOA_SCAN_CASE(4)
     BOA_SCAN_CASE(8)
@@ -193,6 +314,25 @@ cudaError_t launch_scan(const float* delta, int ld, int r, const float* dtw, con
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
+}
+
+// attributes for >48 KB dynamic shared memory, set once per device
+cudaError_t scan_prepare_device() {
+  const int big = 227 * 1024;
+  cudaError_t e;
+#define BOA_ATTR(RR)                                                                                          \
+  if ((e = cudaFuncSetAttribute(scan_step_kernel<RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, big)) != \
+      cudaSuccess)                                                                                            \
+    return e;                                                                                                 \
+  if ((e = cudaFuncSetAttribute(scan_tile_kernel<RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, big)) != \
+      cudaSuccess)                                                                                            \
+    return e;
+  BOA_ATTR(4)
+  BOA_ATTR(8)
+  BOA_ATTR(16)
+  BOA_ATTR(32)
+#undef BOA_ATTR
+  return cudaSuccess;
 }
 
 // ---------------------------------------------------------------- minGRU

@@ -96,6 +96,7 @@ struct boa_model {
   float inv_t = 1.0f;
   std::string err;
   cudaStream_t own = nullptr, ext = nullptr;
+  bool has_ext = false;
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;
   int cfg_batch = 0, cfg_tile = 0;
 
@@ -122,6 +123,15 @@ struct boa_model {
   float* logits = nullptr;
   size_t logits_rows = 0;
 
+  // instrumentation
+  bool prof = false;
+  struct Pend { int cls; cudaEvent_t a, b; };
+  std::vector<Pend> pending;
+  std::vector<cudaEvent_t> ev_pool;
+  double prof_ms[BOA_PROF_CLASSES] = {0};
+  uint64_t prof_n[BOA_PROF_CLASSES] = {0};
+  uint64_t launches = 0;
+
   // host-API staging (grow-only)
   void* io = nullptr;
   size_t io_bytes = 0;
@@ -137,6 +147,8 @@ struct boa_model {
 boa_model::~boa_model() {
   cudaSetDevice(device);
   if (own) cudaStreamSynchronize(own);
+  for (auto& p : pending) { cudaEventDestroy(p.a); cudaEventDestroy(p.b); }
+  for (auto e : ev_pool) cudaEventDestroy(e);
   if (warena) cudaFree(warena);
   if (work) cudaFree(work);
   if (io) cudaFree(io);
@@ -161,15 +173,54 @@ int cuda_fail(boa_model* m, cudaError_t e, const char* where) {
     if (e_ != cudaSuccess) return cuda_fail(m, e_, #call); \
   } while (0)
 
+// Kernel classes for the instrumentation counters.
+enum ProfClass {
+  PC_EMBED = 0, PC_IN_PROJ, PC_CONV, PC_X_PROJ, PC_SCAN, PC_OUT_PROJ_LN, PC_FF1, PC_FF2_LN, PC_HEAD1, PC_HEAD2_CODER,
+  PC_ENCODE, PC_OTHER
+};
+const char* const kProfNames[BOA_PROF_CLASSES] = {"embed_ln", "in_proj", "conv", "x_proj", "scan", "out_proj_ln",
+                                                  "ff1_gelu", "ff2_res_ln", "head1", "head2_coder", "encode_tile",
+                                                  "other"};
+
+cudaEvent_t pool_event(boa_model* m) {
+  if (!m->ev_pool.empty()) { cudaEvent_t e = m->ev_pool.back(); m->ev_pool.pop_back(); return e; }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// Brackets one launch: counts it and, when profiling, records events.
+struct Launch {
+  boa_model* m;
+  int cls;
+  cudaEvent_t a = nullptr;
+  Launch(boa_model* mm, int c) : m(mm), cls(c) {
+    m->launches++;
+    if (m->prof) { a = pool_event(m); cudaEventRecord(a, m->own); }
+  }
+  ~Launch() {
+    if (a) {
+      cudaEvent_t b = pool_event(m);
+      cudaEventRecord(b, m->own);
+      m->pending.push_back({cls, a, b});
+    }
+  }
+};
+#define BOA_LAUNCH(cls, call)    \
+  do {                           \
+    Launch l_(m, cls);           \
+    BOA_CK(call);                \
+  } while (0)
+
 // Entry / exit ordering with an external stream.
 struct StreamScope {
   boa_model* m;
   explicit StreamScope(boa_model* mm) : m(mm) {
     cudaSetDevice(m->device);
-    if (m->ext) { cudaEventRecord(m->ev_in, m->ext); cudaStreamWaitEvent(m->own, m->ev_in, 0); }
+    if (m->has_ext) { cudaEventRecord(m->ev_in, m->ext); cudaStreamWaitEvent(m->own, m->ev_in, 0); }
   }
   ~StreamScope() {
-    if (m->ext) { cudaEventRecord(m->ev_out, m->own); cudaStreamWaitEvent(m->ext, m->ev_out, 0); }
+    if (m->has_ext) { cudaEventRecord(m->ev_out, m->own); cudaStreamWaitEvent(m->ext, m->ev_out, 0); }
   }
 };
 
@@ -255,7 +306,7 @@ int forward(boa_model* m, const boa::TokenSrc& src, int B, int T, int head_mode,
   bf16* hhl = reinterpret_cast<bf16*>(m->xz);   // FF hidden aliases xz (dead after the scan)
   bf16* headh = reinterpret_cast<bf16*>(m->u);  // head hidden aliases u
   const long long head_plane = (long long)m->rows_cap * d;
-  BOA_CK(boa::launch_embed_ln(src, m->emb, d, m->x, m->xn, xn_plane, m->layers[0].ln1w, m->layers[0].ln1b, M, st));
+  BOA_LAUNCH(PC_EMBED, boa::launch_embed_ln(src, m->emb, d, m->x, m->xn, xn_plane, m->layers[0].ln1w, m->layers[0].ln1b, M, st));
   for (int l = 0; l < m->L; ++l) {
     const LayerW& w = m->layers[l];
     const bool last = l + 1 == m->L;
@@ -265,41 +316,41 @@ int forward(boa_model* m, const boa::TokenSrc& src, int B, int T, int head_mode,
       float* cst = m->conv_st + (size_t)l * m->chunks_cap * 3 * di;
       float* sst = m->ssm_st + (size_t)l * m->chunks_cap * 16 * di;
       a.N = 2 * di; a.K = d; a.bias = w.in_b; a.out_f32 = m->xz; a.ld_f32 = 2 * di;
-      BOA_CK(boa::gemm_launch(boa::EPI_F32, m->xn, xn_plane, 0, w.in.p, w.in.plane, a, st));
-      BOA_CK(boa::launch_conv(m->xz, di, cst, w.conv_w, w.conv_b, m->u, m->uhl, u_plane, B, T, st));
+      BOA_LAUNCH(PC_IN_PROJ, boa::gemm_launch(boa::EPI_F32, m->xn, xn_plane, 0, w.in.p, w.in.plane, a, st));
+      BOA_LAUNCH(PC_CONV, boa::launch_conv(m->xz, di, cst, w.conv_w, w.conv_b, m->u, m->uhl, u_plane, B, T, st));
       a = boa::GemmArgs{}; a.M = M;
       a.N = m->xpN; a.K = di; a.out_f32 = m->delta; a.ld_f32 = m->xpN;
-      BOA_CK(boa::gemm_launch(boa::EPI_F32, m->uhl, u_plane, 0, w.xp.p, w.xp.plane, a, st));
-      BOA_CK(boa::launch_scan(m->delta, m->xpN, m->r, w.dt_w, w.dt_b, w.negA, w.Dv, m->u, m->xz, di, sst, m->uhl,
+      BOA_LAUNCH(PC_X_PROJ, boa::gemm_launch(boa::EPI_F32, m->uhl, u_plane, 0, w.xp.p, w.xp.plane, a, st));
+      BOA_LAUNCH(PC_SCAN, boa::launch_scan(m->delta, m->xpN, m->r, w.dt_w, w.dt_b, w.negA, w.Dv, m->u, m->xz, di, sst, m->uhl,
                               u_plane, B, T, st));
       a = boa::GemmArgs{}; a.M = M;
       a.N = d; a.K = di; a.bias = w.out_b; a.out_hl = m->xn; a.ld_hl = d; a.plane_hl = xn_plane;
       a.ln_w = w.ln2w; a.ln_b = w.ln2b;
-      BOA_CK(boa::gemm_launch(boa::EPI_LN_SPLIT, m->uhl, u_plane, 0, w.out.p, w.out.plane, a, st));
+      BOA_LAUNCH(PC_OUT_PROJ_LN, boa::gemm_launch(boa::EPI_LN_SPLIT, m->uhl, u_plane, 0, w.out.p, w.out.plane, a, st));
     } else {
       float* hst = m->h_st + (size_t)l * m->chunks_cap * d;
       a.N = 2 * d; a.K = d; a.bias = w.zh_b; a.out_f32 = m->xz; a.ld_f32 = 2 * d;
-      BOA_CK(boa::gemm_launch(boa::EPI_F32, m->xn, xn_plane, 0, w.zh.p, w.zh.plane, a, st));
-      BOA_CK(boa::launch_mingru(m->xz, d, hst, m->u, B, T, st));
-      BOA_CK(boa::launch_add_ln(m->x, m->u, d, m->xn, xn_plane, w.ln2w, w.ln2b, M, st));
+      BOA_LAUNCH(PC_IN_PROJ, boa::gemm_launch(boa::EPI_F32, m->xn, xn_plane, 0, w.zh.p, w.zh.plane, a, st));
+      BOA_LAUNCH(PC_SCAN, boa::launch_mingru(m->xz, d, hst, m->u, B, T, st));
+      BOA_LAUNCH(PC_OTHER, boa::launch_add_ln(m->x, m->u, d, m->xn, xn_plane, w.ln2w, w.ln2b, M, st));
     }
     a = boa::GemmArgs{}; a.M = M;
     a.N = 4 * d; a.K = d; a.bias = w.ff1_b; a.out_hl = hhl; a.ld_hl = 4 * d; a.plane_hl = h_plane;
     a.act = boa::ACT_GELU;
-    BOA_CK(boa::gemm_launch(boa::EPI_ACT_SPLIT, m->xn, xn_plane, 0, w.ff1.p, w.ff1.plane, a, st));
+    BOA_LAUNCH(PC_FF1, boa::gemm_launch(boa::EPI_ACT_SPLIT, m->xn, xn_plane, 0, w.ff1.p, w.ff1.plane, a, st));
     a = boa::GemmArgs{}; a.M = M;
     a.N = d; a.K = 4 * d; a.bias = w.ff2_b; a.res = m->x; a.out_hl = m->xn; a.ld_hl = d; a.plane_hl = xn_plane;
     if (!last) { a.ln_w = m->layers[l + 1].ln1w; a.ln_b = m->layers[l + 1].ln1b; }
-    BOA_CK(boa::gemm_launch(boa::EPI_RES_LN, hhl, h_plane, 0, w.ff2.p, w.ff2.plane, a, st));
+    BOA_LAUNCH(PC_FF2_LN, boa::gemm_launch(boa::EPI_RES_LN, hhl, h_plane, 0, w.ff2.p, w.ff2.plane, a, st));
   }
   if (m->backbone != BOA_BACKBONE_MAMBA)
-    BOA_CK(boa::launch_rms_split(m->x, d, m->final_norm, m->xn, xn_plane, M, st));
+    BOA_LAUNCH(PC_OTHER, boa::launch_rms_split(m->x, d, m->final_norm, m->xn, xn_plane, M, st));
   boa::GemmArgs a{};
   a.M = M; a.N = d; a.K = d; a.bias = m->h1_b; a.out_hl = headh; a.ld_hl = d; a.plane_hl = head_plane;
   a.act = m->backbone == BOA_BACKBONE_MAMBA ? boa::ACT_RELU : boa::ACT_SILU;
-  BOA_CK(boa::gemm_launch(boa::EPI_ACT_SPLIT, m->xn, xn_plane, 0, m->h1.p, m->h1.plane, a, st));
+  BOA_LAUNCH(PC_HEAD1, boa::gemm_launch(boa::EPI_ACT_SPLIT, m->xn, xn_plane, 0, m->h1.p, m->h1.plane, a, st));
   head.M = M; head.N = 256; head.K = d; head.bias = m->h2_b; head.inv_t = m->inv_t;
-  BOA_CK(boa::gemm_launch(head_mode, headh, head_plane, 0, m->h2.p, m->h2.plane, head, st));
+  BOA_LAUNCH(PC_HEAD2_CODER, boa::gemm_launch(head_mode, headh, head_plane, 0, m->h2.p, m->h2.plane, head, st));
   return 0;
 }
 
@@ -489,7 +540,7 @@ int boa_model_load(const char* path, int backbone, int d, int nl, int device, bo
   }
   if (fnorm >= 0) m->final_norm = fp[fnorm];
   m->h1 = hp[h1]; m->h1_b = fp[h1b]; m->h2 = hp[h2]; m->h2_b = fp[h2b];
-  if ((e = boa::gemm_prepare_device()) != cudaSuccess)
+  if ((e = boa::gemm_prepare_device()) != cudaSuccess || (e = boa::scan_prepare_device()) != cudaSuccess)
     return fail(nullptr, BOA_E_CUDA, std::string("GEMM kernel setup: ") + cudaGetErrorString(e));
   if ((e = cudaStreamCreateWithFlags(&m->own, cudaStreamNonBlocking)) != cudaSuccess ||
       (e = cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming)) != cudaSuccess ||
@@ -511,6 +562,7 @@ int boa_set_temperature(boa_model* m, float t) {
 int boa_set_stream(boa_model* m, void* s) {
   if (!m) return BOA_E_INVALID;
   m->ext = (cudaStream_t)s;
+  m->has_ext = true;
   return 0;
 }
 
@@ -530,7 +582,7 @@ int boa_sync(boa_model* m) {
   if (!m) return BOA_E_INVALID;
   cudaSetDevice(m->device);
   BOA_CK(cudaStreamSynchronize(m->own));
-  if (m->ext) BOA_CK(cudaStreamSynchronize(m->ext));
+  if (m->has_ext) BOA_CK(cudaStreamSynchronize(m->ext));
   return read_dev_error(m);
 }
 
@@ -554,19 +606,19 @@ int boa_compress_device(boa_model* m, const uint8_t* d_data, uint64_t n, uint32_
     const uint8_t* data = d_data + (size_t)c0 * chunk_len;
     const long long rem = (long long)(n - (uint64_t)c0 * chunk_len);
     if (int rc = reset_states(m, Bb)) return rc;
-    BOA_CK(boa::launch_enc_init(m->es, Bb, st));
-    BOA_CK(boa::launch_first_bytes(data, rem, chunk_len, d_first + c0, Bb, st));
+    BOA_LAUNCH(PC_OTHER, boa::launch_enc_init(m->es, Bb, st));
+    BOA_LAUNCH(PC_OTHER, boa::launch_first_bytes(data, rem, chunk_len, d_first + c0, Bb, st));
     const int max_len = (int)std::min<long long>(chunk_len, rem);
     for (int t0 = 0; t0 < max_len - 1; t0 += T) {
       boa::TokenSrc src{1, data, rem, (int)chunk_len, t0, T, nullptr};
       boa::GemmArgs h{};
       h.tokens = data; h.n_bytes = rem; h.chunk_len = (int)chunk_len; h.t0 = t0; h.T = T; h.lf = m->lf;
       if (int rc = forward(m, src, Bb, T, boa::EPI_HEAD_ENC, h)) return rc;
-      BOA_CK(boa::launch_encode_tile(m->lf, m->es, m->pitch_buf, (int)pitch, Bb, T, t0, rem, (int)chunk_len, st));
+      BOA_LAUNCH(PC_ENCODE, boa::launch_encode_tile(m->lf, m->es, m->pitch_buf, (int)pitch, Bb, T, t0, rem, (int)chunk_len, st));
     }
-    BOA_CK(boa::launch_enc_finish(m->es, m->pitch_buf, (int)pitch, d_sizes + c0, Bb, st));
-    BOA_CK(boa::launch_offsets(d_sizes + c0, (unsigned long long*)d_offsets + c0, Bb, st));
-    BOA_CK(boa::launch_compact(m->pitch_buf, (int)pitch, d_sizes + c0, (unsigned long long*)d_offsets + c0, d_payload,
+    BOA_LAUNCH(PC_OTHER, boa::launch_enc_finish(m->es, m->pitch_buf, (int)pitch, d_sizes + c0, Bb, st));
+    BOA_LAUNCH(PC_OTHER, boa::launch_offsets(d_sizes + c0, (unsigned long long*)d_offsets + c0, Bb, st));
+    BOA_LAUNCH(PC_OTHER, boa::launch_compact(m->pitch_buf, (int)pitch, d_sizes + c0, (unsigned long long*)d_offsets + c0, d_payload,
                                Bb, st));
   }
   return 0;
@@ -587,23 +639,33 @@ int boa_decompress_device(boa_model* m, const uint32_t* d_payload, const uint64_
     const long long rem = (long long)(n - (uint64_t)c0 * chunk_len);
     uint8_t* out = d_out + (size_t)c0 * chunk_len;
     if (int rc = reset_states(m, Bb)) return rc;
-    BOA_CK(boa::launch_dec_init(m->ds, d_payload, (const unsigned long long*)d_offsets + c0, d_sizes + c0,
+    BOA_LAUNCH(PC_OTHER, boa::launch_dec_init(m->ds, d_payload, (const unsigned long long*)d_offsets + c0, d_sizes + c0,
                                 d_first + c0, out, rem, chunk_len, Bb, st));
-    BOA_CK(boa::launch_set_counter(m->d_t, 1, st));
+    BOA_LAUNCH(PC_OTHER, boa::launch_set_counter(m->d_t, 1, st));
     const int max_len = (int)std::min<long long>(chunk_len, rem);
     if (max_len <= 1) continue;
-    // capture one step (model + fused decode + counter) and replay it
-    // max_len - 1 times (boa.cpp:736-756)
-    cudaGraph_t graph = nullptr;
-    cudaGraphExec_t exec = nullptr;
-    BOA_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
     boa::TokenSrc src{2, out, rem, (int)chunk_len, 0, 1, m->d_t};
     boa::GemmArgs h{};
     h.out_bytes = out; h.n_bytes = rem; h.chunk_len = (int)chunk_len; h.d_t = m->d_t; h.dstates = m->ds;
     h.payload = d_payload; h.offsets = (const unsigned long long*)d_offsets + c0;
+    if (m->prof) {  // eager steps so every launch is bracketed by events
+      for (int t = 1; t < max_len; ++t) {
+        if (int rc = forward(m, src, Bb, 1, boa::EPI_HEAD_DEC, h)) return rc;
+        BOA_LAUNCH(PC_OTHER, boa::launch_increment(m->d_t, st));
+      }
+      continue;
+    }
+    // capture one step (model + fused decode + counter) and replay it
+    // max_len - 1 times (boa.cpp:736-756)
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    const uint64_t l0 = m->launches;
+    BOA_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
     int rc = forward(m, src, Bb, 1, boa::EPI_HEAD_DEC, h);
     cudaError_t ei = boa::launch_increment(m->d_t, st);
     cudaError_t ee = cudaStreamEndCapture(st, &graph);
+    const uint64_t per_step = m->launches - l0 + 1;
+    m->launches = l0;
     if (rc) { if (graph) cudaGraphDestroy(graph); return rc; }
     if (ei != cudaSuccess) { if (graph) cudaGraphDestroy(graph); return cuda_fail(m, ei, "capture increment"); }
     if (ee != cudaSuccess) return cuda_fail(m, ee, "cudaStreamEndCapture");
@@ -613,6 +675,7 @@ int boa_decompress_device(boa_model* m, const uint32_t* d_payload, const uint64_
     for (int t = 1; t < max_len; ++t) {
       e = cudaGraphLaunch(exec, st);
       if (e != cudaSuccess) break;
+      m->launches += per_step;
     }
     cudaGraphExecDestroy(exec);
     if (e != cudaSuccess) return cuda_fail(m, e, "cudaGraphLaunch");
@@ -692,6 +755,39 @@ int boa_decompress_chunks(boa_model* m, const uint32_t* payload, const uint32_t*
   BOA_CK(cudaMemcpyAsync(out, d_out, nb, cudaMemcpyDeviceToHost, m->own));
   BOA_CK(cudaStreamSynchronize(m->own));
   return read_dev_error(m);
+}
+
+int boa_set_profiling(boa_model* m, int on) {
+  if (!m) return BOA_E_INVALID;
+  m->prof = on != 0;
+  return 0;
+}
+
+const char* boa_profile_name(int c) { return (c >= 0 && c < BOA_PROF_CLASSES) ? kProfNames[c] : nullptr; }
+
+uint64_t boa_launch_count(const boa_model* m) { return m ? m->launches : 0; }
+
+int boa_profile_read(boa_model* m, int c, double* total_ms, uint64_t* n) {
+  if (!m) return BOA_E_INVALID;
+  if (c < 0 || c >= BOA_PROF_CLASSES) return fail(m, BOA_E_INVALID, "kernel class out of range");
+  if (!m->pending.empty()) {
+    cudaSetDevice(m->device);
+    BOA_CK(cudaStreamSynchronize(m->own));
+    for (auto& p : m->pending) {
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, p.a, p.b);
+      m->prof_ms[p.cls] += ms;
+      m->prof_n[p.cls] += 1;
+      m->ev_pool.push_back(p.a);
+      m->ev_pool.push_back(p.b);
+    }
+    m->pending.clear();
+  }
+  if (total_ms) *total_ms = m->prof_ms[c];
+  if (n) *n = m->prof_n[c];
+  m->prof_ms[c] = 0.0;
+  m->prof_n[c] = 0;
+  return 0;
 }
 
 int boa_model_logits(boa_model* m, const uint8_t* tokens, int B, int L, int mode, float* logits) {

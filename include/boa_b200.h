@@ -54,9 +54,11 @@ const char* boa_last_error(const boa_model* h);
 /* Replaces gpu_set_temperature (range_coder_kernels.cu:9-12): logits are
  * scaled by 1/T (computed in fp32) before the softmax. */
 int boa_set_temperature(boa_model* h, float temperature);
-/* Replaces the global g_stream (utility_kernels.cu:5): work is ordered after
- * prior work on `cuda_stream` and later work on it waits for the library.
- * NULL restores the handle's private stream. */
+/* Replaces the global g_stream (utility_kernels.cu:5): after this call, work
+ * of the handle is ordered after prior work on `cuda_stream` and later work
+ * on `cuda_stream` waits for it.  NULL names the legacy default stream (it is
+ * an external stream like any other).  Without this call the handle runs on
+ * its private stream and callers use boa_sync(). */
 int boa_set_stream(boa_model* h, void* cuda_stream);
 /* Chunks per batch (--gpu-batch, boa.cpp:310) and tokens per compress tile
  * (--tile, boa.cpp:313-316).  0 = automatic from free device memory
@@ -99,6 +101,19 @@ int boa_decompress_device(boa_model* h, const uint32_t* d_payload, const uint64_
 int boa_sync(boa_model* h);
 /* Device memory the handle holds (weights + work buffers + states). */
 uint64_t boa_device_bytes(const boa_model* h);
+
+/* ---- instrumentation (the reference's --show-timings, boa.cpp:376-506) ---
+ * With profiling on, every kernel launch of the handle is bracketed by CUDA
+ * events on the stream it runs on and the decompress step runs without graph
+ * capture; boa_profile_read() synchronises and reports, per kernel class,
+ * the summed device time and the number of launches since the last read.
+ * boa_launch_count() counts every kernel the handle has launched (graph
+ * replays included), profiling or not. */
+#define BOA_PROF_CLASSES 12
+int boa_set_profiling(boa_model* h, int on);
+int boa_profile_read(boa_model* h, int kernel_class, double* total_ms, uint64_t* launches);
+const char* boa_profile_name(int kernel_class);
+uint64_t boa_launch_count(const boa_model* h);
 
 /* ---- model outputs for parity testing ------------------------------------
  * Logits [B][L][256] (head bias included) of B fresh chunks of L tokens.
