@@ -80,6 +80,8 @@ SIGNATURES = {
     "boa_model_logits": (C.c_int, [C.c_void_p, _u8p, C.c_int, C.c_int, C.c_int, _f32p]),
     "boa_rc_encode_cdf": (C.c_int, [C.c_void_p, _u32p, _u8p, C.c_int, C.c_int, _u32p, C.c_size_t, _u32p]),
     "boa_rc_decode_cdf": (C.c_int, [C.c_void_p, _u32p, C.c_int, C.c_int, _u32p, _u32p, _u8p]),
+    "boa_rc_encode_cdf_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_uint32,
+                                            C.c_void_p, C.c_void_p]),
     "boa_cdf_from_logits": (C.c_int, [C.c_void_p, _f32p, C.c_int, C.c_float, _u32p]),
     "boa_boa2_build": (C.c_int, [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _u8p,
                                  _u64p, _u8p, _u8p, C.c_size_t, C.POINTER(C.c_size_t)]),

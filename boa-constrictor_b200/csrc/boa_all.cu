@@ -6,3 +6,4 @@
 #include "mamba.cu"
 #include "runtime.cpp"
 #include "container.cpp"
+#include "noalloc.cu"

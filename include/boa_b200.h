@@ -135,6 +135,22 @@ int boa_rc_encode_cdf(boa_model* h, const uint32_t* cdf, const uint8_t* syms, in
                       uint32_t* payload, size_t payload_cap_words, uint32_t* sizes_words);
 int boa_rc_decode_cdf(boa_model* h, const uint32_t* cdf, int n_streams, int n_steps, const uint32_t* payload,
                       const uint32_t* sizes_words, uint8_t* syms);
+/* The encoder above without any allocation, for callers that cannot allocate
+ * device memory where they encode (a pooled or framework-owned allocator that
+ * forbids raw cudaMalloc, a plugin that must keep its memory footprint fixed).
+ * No counterpart in the reference.  All pointers are device pointers: the
+ * same cdf/syms layout as boa_rc_encode_cdf; stream i is written to
+ * d_words + i*pitch_words (pitch_words >= boa_stream_capacity_words(n_steps+1))
+ * and its word count to d_sizes[i].  The per-stream coder states live in one
+ * static device array of 65536 x 32 bytes (2 MiB), held by every GPU that
+ * loads the library until exit; n_streams above 65536 is rejected.  Work is
+ * enqueued on `stream` (NULL = legacy default stream) and nothing is
+ * synchronised.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress), so make it before any stream capture.
+ * Every call shares the array and resets the states it uses: calls that
+ * overlap on the GPU race.  Errors are reported by boa_last_error(NULL). */
+int boa_rc_encode_cdf_noalloc(const uint32_t* d_cdf, const uint8_t* d_syms, int n_streams, int n_steps,
+                              uint32_t* d_words, uint32_t pitch_words, uint32_t* d_sizes, void* stream);
 /* The integer CDF the library derives from one or more logits rows
  * ([rows][256] -> [rows][257]); exposes the quantiser of
  * range_coder_kernels.cu:860-925 for testing.  Host buffers. */
