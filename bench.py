@@ -314,16 +314,16 @@ def main():
     e2e_step_ms = te.item()
 
     # ---- per-kernel timing: instrumented pass (events around every launch)
-    # over one compress tile and 8 decode steps of the same C chunks
+    # over one compress tile and T decode steps of the same C chunks
     m.set_profiling(True)
     m.profile()
-    T = 64
+    T = min(64, max(1, S - 1))
     tl = T + 1
     tdata = data.view(C, S)[:, :tl].contiguous().view(-1)
     m.compress_device(tdata.data_ptr(), C * tl, tl, C, first.data_ptr(), payload.data_ptr(), cap,
                       sizes.data_ptr(), offsets.data_ptr())
     prof_c = m.profile()
-    m.decompress_device(payload.data_ptr(), offsets.data_ptr(), sizes.data_ptr(), first.data_ptr(), C * 9, 9, C,
+    m.decompress_device(payload.data_ptr(), offsets.data_ptr(), sizes.data_ptr(), first.data_ptr(), C * tl, tl, C,
                         out.data_ptr())
     prof_d = m.profile()
     m.set_profiling(False)
@@ -335,10 +335,10 @@ def main():
         dms, dn = prof_d[name]
         kern[name] = {"compress_ms_per_launch": cms / cn if cn else 0.0, "compress_launches": cn,
                       "decode_ms_per_launch": dms / dn if dn else 0.0, "decode_launches": dn,
-                      "est_ms_per_step": (cms * steps_c + dms / 8 * steps_d)}
+                      "est_ms_per_step": (cms * steps_c + dms / (tl - 1) * steps_d)}
     dom = max(kern, key=lambda k: kern[k]["est_ms_per_step"])
     kd = kern[dom]
-    in_decode = kd["decode_ms_per_launch"] * kd["decode_launches"] / 8 * steps_d >= kd["compress_ms_per_launch"] * kd["compress_launches"] * steps_c
+    in_decode = kd["decode_ms_per_launch"] * kd["decode_launches"] / (tl - 1) * steps_d >= kd["compress_ms_per_launch"] * kd["compress_launches"] * steps_c
     if in_decode:
         bound, work = algorithmic_per_launch(dom, C, 1, a.d_model, a.layers)
         dur = kd["decode_ms_per_launch"]

@@ -37,10 +37,15 @@ struct GemmCfg {
   static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
+// GELU (tanh form, activations.hpp:105-118) with tanh(u) = 1 - 2 / (1 + e^{2u})
+// from the MUFU exponential: a few instructions instead of an accurate tanhf,
+// ~1e-6 relative, deterministic.
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == ACT_GELU) {
     const float k0 = 0.79788456080286535588f, k1 = 0.044715f;
-    return 0.5f * v * (1.0f + tanhf(k0 * (v + k1 * v * v * v)));
+    const float u = k0 * (v + k1 * v * v * v);
+    const float th = 1.0f - __fdividef(2.0f, 1.0f + __expf(2.0f * u));
+    return 0.5f * v * (1.0f + th);
   }
   if (act == ACT_RELU) return fmaxf(0.0f, v);
   if (act == ACT_SILU) return v / (1.0f + __expf(-v));
@@ -288,27 +293,106 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   }
 }
 
+// Per-warp 32-row x 16-column staging tile.  The epilogue thread owns one
+// accumulator row; global traffic goes through the tile so that every warp
+// access covers 8 rows x 64 contiguous bytes with 128-bit operations.  Row
+// stride 20 floats keeps 16-byte alignment and conflict-free 128-bit stores.
+constexpr int kTileStride = 20;
+__device__ __forceinline__ void tile_put_row(float* wb, int lane, const float (&v)[16]) {
+  float4* p = reinterpret_cast<float4*>(wb + lane * kTileStride);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) p[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  __syncwarp();
+}
+__device__ __forceinline__ void tile_get_row(const float* wb, int lane, float (&v)[16]) {
+  const float4* p = reinterpret_cast<const float4*>(wb + lane * kTileStride);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float4 t = p[j];
+    v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+  }
+  __syncwarp();
+}
+// lane -> (row r = it*8 + lane/4, columns 4*(lane%4) .. +3)
+__device__ __forceinline__ void tile_store_f32(const float* wb, int lane, float* g, size_t ld, int nrows) {
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int r = it * 8 + (lane >> 2), cc = (lane & 3) * 4;
+    if (r < nrows)
+      *reinterpret_cast<float4*>(g + (size_t)r * ld + cc) = *reinterpret_cast<const float4*>(wb + r * kTileStride + cc);
+  }
+  __syncwarp();
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo_col, float hi_col) {
+  __nv_bfloat162 t = __floats2bfloat162_rn(lo_col, hi_col);  // .x = lo_col (lower address)
+  return *reinterpret_cast<uint32_t*>(&t);
+}
+__device__ __forceinline__ float bf16_lo_half(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16_hi_half(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+__device__ __forceinline__ void tile_store_split(const float* wb, int lane, __nv_bfloat16* g, long long plane, size_t ld,
+                                                 int nrows) {
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int r = it * 8 + (lane >> 2), cc = (lane & 3) * 4;
+    if (r < nrows) {
+      const float4 v = *reinterpret_cast<const float4*>(wb + r * kTileStride + cc);
+      // hi = bf16(v), lo = bf16(v - hi): the same values as split_bf16
+      const uint32_t h01 = pack_bf16x2(v.x, v.y), h23 = pack_bf16x2(v.z, v.w);
+      const uint32_t l01 = pack_bf16x2(v.x - bf16_lo_half(h01), v.y - bf16_hi_half(h01));
+      const uint32_t l23 = pack_bf16x2(v.z - bf16_lo_half(h23), v.w - bf16_hi_half(h23));
+      __nv_bfloat16* gp = g + (size_t)r * ld + cc;
+      *reinterpret_cast<uint2*>(gp) = make_uint2(h01, h23);
+      *reinterpret_cast<uint2*>(gp + plane) = make_uint2(l01, l23);
+    }
+  }
+  __syncwarp();
+}
+__device__ __forceinline__ void tile_load_f32(float* wb, int lane, const float* g, size_t ld, int nrows) {
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int r = it * 8 + (lane >> 2), cc = (lane & 3) * 4;
+    *reinterpret_cast<float4*>(wb + r * kTileStride + cc) =
+        r < nrows ? *reinterpret_cast<const float4*>(g + (size_t)r * ld + cc) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __syncwarp();
+}
+__device__ __forceinline__ void load_bias16(const float* b, float (&o)[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float4 t = reinterpret_cast<const float4*>(b)[j];
+    o[4 * j] = t.x; o[4 * j + 1] = t.y; o[4 * j + 2] = t.z; o[4 * j + 3] = t.w;
+  }
+}
+
 // ------------------------------------------------------------------ persistent
 // Persistent form for the row-parallel epilogues (F32, ACT_SPLIT, LN_SPLIT,
 // RES_LN): one CTA per SM walks tiles t = blockIdx.x, +gridDim.x, ...; two
 // TMEM accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
 //   warp 0      TMA producer (continuous across tiles)
 //   warp 1      TMEM allocator + MMA issuer
-//   warps 2..9  epilogue; warp w reads TMEM lane quarter w % 4 and column
-//               half (w - 2) / 4.  LayerNorm moments are combined across the
-//               two halves in a fixed order (half 0 + half 1).
-constexpr int kPThreads = 320;
-constexpr int kEpiThreads = 256;
+//   warps 2..17 epilogue; warp w reads TMEM lane quarter w % 4 and column
+//               quarter (w - 2) / 4.  LayerNorm moments are combined across
+//               the four column parts in a fixed order.
+constexpr int kEpiWarps = 16;
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kPThreads = 64 + kEpiThreads;
 
+// K-block of 32 (64-byte rows, 64-byte swizzle) for wide tiles so four or more
+// stages fit and cover TMA latency; 64 (128-byte swizzle) for narrow ones.
 template <int BN>
 struct PCfg {
-  static constexpr int kStages = BN >= 256 ? 2 : (BN >= 128 ? 3 : 4);
+  static constexpr int kBK = BN >= 128 ? 32 : 64;
+  static constexpr int kSwz = kBK * 2;  // swizzle span in bytes (64 or 128)
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;
+  static constexpr int kEpiBuf = kEpiWarps * 32 * kTileStride * 4;  // staging tiles
+  static constexpr int kRed = kBM * 4 * 2 * 4;
+  static constexpr int kBudget = 225 * 1024 - 1024 - 256 - kRed - kEpiBuf;
+  static constexpr int kStages = kBudget / kStageBytes > 8 ? 8 : kBudget / kStageBytes;
   static constexpr int kAccCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr int kTmemCols = 2 * kAccCols;
-  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256 + kBM * 2 * 2 * 4;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256 + kRed + kEpiBuf;
 };
 
 template <int BN, int MODE>
@@ -324,16 +408,17 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   uint64_t* acc_empty = bars + 2 * Cfg::kStages + 2;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * Cfg::kStages + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* red = reinterpret_cast<float*>(smem + Cfg::kStages * Cfg::kStageBytes + 256);  // [128][2 halves][2]
+  float* red = reinterpret_cast<float*>(smem + Cfg::kStages * Cfg::kStageBytes + 256);  // [128][4 parts][2]
+  float* ebuf = red + kBM * 4 * 2;  // [kEpiWarps][32][kTileStride]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles_n = args.N / BN;
   const int n_tiles = n_tiles_n * ((args.M + kBM - 1) / kBM);
-  const int nkb = (args.K + kBK - 1) / kBK;
+  const int nkb = (args.K + Cfg::kBK - 1) / Cfg::kBK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int a = 0; a < 2; ++a) { mbar_init(&acc_full[a], 1); mbar_init(&acc_empty[a], kEpiThreads / 32); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&acc_full[a], 1); mbar_init(&acc_empty[a], kEpiWarps); }
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
@@ -355,7 +440,7 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           if (g >= Cfg::kStages && !mbar_wait(&empty[s], ((g / Cfg::kStages) - 1) & 1)) { *abort_flag = 1; break; }
           uint8_t* st = smem + s * Cfg::kStageBytes;
           mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-          const int k0 = kb * kBK;
+          const int k0 = kb * Cfg::kBK;
           tma_load_3d(st, &tmA, &full[s], k0, m0, 0);
           tma_load_3d(st + Cfg::kABytes, &tmA, &full[s], k0, m0, 1);
           tma_load_3d(st + 2 * Cfg::kABytes, &tmW, &full[s], k0, n0, 0);
@@ -378,12 +463,12 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           if (!mbar_wait(&full[s], (g / Cfg::kStages) & 1)) { *abort_flag = 1; break; }
           tc_fence_after();
           const uint32_t st = smem_u32(smem + s * Cfg::kStageBytes);
-          const uint64_t dAh = umma_desc_sw128(st);
-          const uint64_t dAl = umma_desc_sw128(st + Cfg::kABytes);
-          const uint64_t dWh = umma_desc_sw128(st + 2 * Cfg::kABytes);
-          const uint64_t dWl = umma_desc_sw128(st + 2 * Cfg::kABytes + Cfg::kBBytes);
+          const uint64_t dAh = umma_desc_swz<Cfg::kSwz>(st);
+          const uint64_t dAl = umma_desc_swz<Cfg::kSwz>(st + Cfg::kABytes);
+          const uint64_t dWh = umma_desc_swz<Cfg::kSwz>(st + 2 * Cfg::kABytes);
+          const uint64_t dWl = umma_desc_swz<Cfg::kSwz>(st + 2 * Cfg::kABytes + Cfg::kBBytes);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
+          for (int kk = 0; kk < Cfg::kBK / 16; ++kk) {
             const uint64_t adv = (uint64_t)(kk * 32 >> 4);
             umma_bf16(acc, dAh + adv, dWh + adv, idesc, (kb | kk) != 0);
             umma_bf16(acc, dAh + adv, dWl + adv, idesc, 1u);
@@ -397,11 +482,10 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     }
   } else {
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int part = (warp - 2) >> 2;  // column quarter 0..3
     const int r_local = q * 32 + lane;
-    // column range of this half in whole 16-column chunks (BN = 48 -> 32 + 16)
+    // column range of this part in whole 16-column chunks
     constexpr int kChunks = BN / 16;
-    constexpr int kChunks0 = (kChunks + 1) / 2;
     int it = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
       const int a = it & 1;
@@ -411,33 +495,46 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       const bool ok = mbar_wait(&acc_full[a], (it >> 1) & 1);
       tc_fence_after();
       if (!ok) break;
+#ifdef BOA_EPI_STUB  // experiment builds only: drain the accumulator without an epilogue
+      if (true) { tc_fence_before(); __syncwarp(); if (lane == 0) mbar_arrive(&acc_empty[a]); continue; }
+#endif
       const uint32_t trow = tmem + (uint32_t)(a * Cfg::kAccCols) + ((uint32_t)(q * 32) << 16);
-      const int row = m0 + r_local;
-      const bool live = row < args.M;
-      const int c0 = half ? kChunks0 * 16 : 0;
-      const int c1 = half ? BN : kChunks0 * 16;
+      const int c0 = (kChunks * part) / 4 * 16;
+      const int c1 = (kChunks * (part + 1)) / 4 * 16;
+      float* wb = ebuf + (warp - 2) * 32 * kTileStride;
+      const int wrow0 = m0 + q * 32;
+      const int nrows = max(0, min(32, args.M - wrow0));
       if constexpr (MODE == EPI_F32) {
 #pragma unroll 1
         for (int c = c0; c < c1; c += 16) {
           float v[16];
           tmem_ld16(trow + c, v);
           if (args.bias) {
+            float bb[16];
+            load_bias16(args.bias + n0 + c, bb);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] += args.bias[n0 + c + j];
+            for (int j = 0; j < 16; ++j) v[j] += bb[j];
           }
-          if (live) store_f32x16(args.out_f32 + (size_t)row * args.ld_f32 + n0 + c, v);
+          tile_put_row(wb, lane, v);
+          tile_store_f32(wb, lane, args.out_f32 + (size_t)wrow0 * args.ld_f32 + n0 + c, args.ld_f32, nrows);
         }
       } else if constexpr (MODE == EPI_ACT_SPLIT) {
 #pragma unroll 1
         for (int c = c0; c < c1; c += 16) {
           float v[16];
           tmem_ld16(trow + c, v);
+          float bb[16];
+          load_bias16(args.bias + n0 + c, bb);
+          if (args.act == ACT_GELU) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = apply_act(v[j] + args.bias[n0 + c + j], args.act);
-          if (live) {
-            __nv_bfloat16* hi = args.out_hl + (size_t)row * args.ld_hl + n0 + c;
-            store_split16(hi, hi + args.plane_hl, v);
+            for (int j = 0; j < 16; ++j) v[j] = apply_act(v[j] + bb[j], ACT_GELU);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = apply_act(v[j] + bb[j], args.act);
           }
+          tile_put_row(wb, lane, v);
+          tile_store_split(wb, lane, args.out_hl + (size_t)wrow0 * args.ld_hl + n0 + c, args.plane_hl, args.ld_hl,
+                           nrows);
         }
       } else {  // EPI_LN_SPLIT / EPI_RES_LN: BN == N, full row in this tile
         float sum = 0.f, sq = 0.f;
@@ -445,23 +542,34 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         for (int c = c0; c < c1; c += 16) {
           float v[16];
           tmem_ld16(trow + c, v);
+          float r[16];
+          if constexpr (MODE == EPI_RES_LN) {
+            tile_load_f32(wb, lane, args.res + (size_t)wrow0 * BN + c, BN, nrows);
+            tile_get_row(wb, lane, r);
+          }
+          float bb[16];
+          load_bias16(args.bias + c, bb);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            float x = v[j] + args.bias[c + j];
-            if constexpr (MODE == EPI_RES_LN) x = x + (live ? args.res[(size_t)row * BN + c + j] : 0.f);
+            float x = v[j] + bb[j];
+            if constexpr (MODE == EPI_RES_LN) x = x + r[j];
             v[j] = x;
             sum += x;
             sq += x * x;
           }
           if constexpr (MODE == EPI_RES_LN) {
-            if (live) store_f32x16(args.res + (size_t)row * BN + c, v);
+            tile_put_row(wb, lane, v);
+            tile_store_f32(wb, lane, args.res + (size_t)wrow0 * BN + c, BN, nrows);
           }
         }
-        red[(r_local * 2 + half) * 2 + 0] = sum;
-        red[(r_local * 2 + half) * 2 + 1] = sq;
+        red[(r_local * 4 + part) * 2 + 0] = sum;
+        red[(r_local * 4 + part) * 2 + 1] = sq;
         named_bar_sync(1, kEpiThreads);
-        sum = red[(r_local * 2 + 0) * 2 + 0] + red[(r_local * 2 + 1) * 2 + 0];
-        sq = red[(r_local * 2 + 0) * 2 + 1] + red[(r_local * 2 + 1) * 2 + 1];
+        // fixed combination order: ((p0 + p1) + p2) + p3
+        sum = ((red[(r_local * 4 + 0) * 2] + red[(r_local * 4 + 1) * 2]) + red[(r_local * 4 + 2) * 2]) +
+              red[(r_local * 4 + 3) * 2];
+        sq = ((red[(r_local * 4 + 0) * 2 + 1] + red[(r_local * 4 + 1) * 2 + 1]) + red[(r_local * 4 + 2) * 2 + 1]) +
+             red[(r_local * 4 + 3) * 2 + 1];
         const bool norm = args.ln_w != nullptr;
         const float mean = sum / (float)BN;
         const float var = sq / (float)BN - mean * mean;
@@ -469,30 +577,26 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 #pragma unroll 1
         for (int c = c0; c < c1; c += 16) {
           float v[16];
+          tmem_ld16(trow + c, v);
           if constexpr (MODE == EPI_RES_LN) {
-            if (live) {
-#pragma unroll
-              for (int j = 0; j < 16; j += 4) {
-                float4 tt = reinterpret_cast<const float4*>(args.res + (size_t)row * BN + c)[j / 4];
-                v[j] = tt.x; v[j + 1] = tt.y; v[j + 2] = tt.z; v[j + 3] = tt.w;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] = 0.f;
-            }
+            // x = acc + bias + residual was stored in pass 1; read it back
+            tile_load_f32(wb, lane, args.res + (size_t)wrow0 * BN + c, BN, nrows);
+            tile_get_row(wb, lane, v);
           } else {
-            tmem_ld16(trow + c, v);
+            float bb[16];
+            load_bias16(args.bias + c, bb);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = v[j] + args.bias[c + j];
+            for (int j = 0; j < 16; ++j) v[j] = v[j] + bb[j];
           }
           if (norm) {
+            float lw[16], lb[16];
+            load_bias16(args.ln_w + c, lw);
+            load_bias16(args.ln_b + c, lb);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = (v[j] - mean) * inv_std * args.ln_w[c + j] + args.ln_b[c + j];
+            for (int j = 0; j < 16; ++j) v[j] = (v[j] - mean) * inv_std * lw[j] + lb[j];
           }
-          if (live) {
-            __nv_bfloat16* hi = args.out_hl + (size_t)row * args.ld_hl + c;
-            store_split16(hi, hi + args.plane_hl, v);
-          }
+          tile_put_row(wb, lane, v);
+          tile_store_split(wb, lane, args.out_hl + (size_t)wrow0 * args.ld_hl + c, args.plane_hl, args.ld_hl, nrows);
         }
         named_bar_sync(1, kEpiThreads);  // red[] reused by the next tile
       }
@@ -527,16 +631,18 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 3-D map over a [2][rows][K] bf16 plane pair, box = 64 (K) x box_rows x 1.
-static bool make_plane_map(CUtensorMap* map, const void* base, int K, int rows, long long plane, int box_rows) {
+// 3-D map over a [2][rows][K] bf16 plane pair, box = box_k (K) x box_rows x 1,
+// swizzle span = box_k * 2 bytes (64 or 128).
+static bool make_plane_map(CUtensorMap* map, const void* base, int K, int rows, long long plane, int box_rows,
+                           int box_k) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, 2};
   cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)plane * 2};
-  cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)box_rows, 1};
+  cuuint32_t box[3] = {(cuuint32_t)box_k, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, box_k == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -627,9 +733,11 @@ cudaError_t gemm_launch(int mode, const __nv_bfloat16* A, long long a_plane, int
   const int BN = pick_bn(mode, args.N);
   if (BN != 48 && BN != 64 && BN != 128 && BN != 256) return cudaErrorInvalidValue;
   if (mode >= EPI_LOGITS && BN != 256) return cudaErrorInvalidValue;
+  // persistent row-parallel modes with BN >= 128 use K-blocks of 32
+  const int box_k = (mode <= EPI_RES_LN && BN >= 128) ? 32 : kBK;
   CUtensorMap ta, tw;
-  if (!make_plane_map(&ta, A, args.K, args.M, a_plane, kBM)) return cudaErrorInvalidValue;
-  if (!make_plane_map(&tw, W, args.K, args.N, w_plane, BN)) return cudaErrorInvalidValue;
+  if (!make_plane_map(&ta, A, args.K, args.M, a_plane, kBM, box_k)) return cudaErrorInvalidValue;
+  if (!make_plane_map(&tw, W, args.K, args.N, w_plane, BN, box_k)) return cudaErrorInvalidValue;
   switch (BN) {
     case 48: return dispatch<48>(mode, ta, tw, args, stream);
     case 64: return dispatch<64>(mode, ta, tw, args, stream);

@@ -5,6 +5,7 @@
 // run identical arithmetic per row.
 #include <algorithm>
 #include "kernels.cuh"
+#include "rowmath.cuh"
 
 namespace boa {
 
@@ -97,23 +98,41 @@ __global__ void conv_kernel(const float* __restrict__ xz, int di, float* __restr
   float w0 = s[0], w1 = s[di], w2 = s[2 * di];
   const float4 k = reinterpret_cast<const float4*>(cw)[c];
   const float bias = cb[c];
-  float xt_next = xz[(size_t)b * T * 2 * di + c];
-  for (int tau = 0; tau < T; ++tau) {
-    const size_t row = (size_t)b * T + tau;
-    const float xt = xt_next;
-    if (tau + 1 < T) xt_next = xz[(row + 1) * 2 * di + c];
-    float v = bias;
-    v = __fadd_rn(v, __fmul_rn(w0, k.x));
-    v = __fadd_rn(v, __fmul_rn(w1, k.y));
-    v = __fadd_rn(v, __fmul_rn(w2, k.z));
-    v = __fadd_rn(v, __fmul_rn(xt, k.w));
-    const float o = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
-    u[row * di + c] = o;
+  if (T == 1) {  // decompress step: one position
+    const float xt = xz[(size_t)b * 2 * di + c];
+    const float o = conv_tap(w0, w1, w2, xt, k, bias);
+    u[(size_t)b * di + c] = o;
     __nv_bfloat16 h, l;
     split_bf16(o, h, l);
-    uhl[row * di + c] = h;
-    uhl[plane + row * di + c] = l;
-    w0 = w1; w1 = w2; w2 = xt;
+    uhl[(size_t)b * di + c] = h;
+    uhl[plane + (size_t)b * di + c] = l;
+    s[0] = w1; s[di] = w2; s[2 * di] = xt;
+    return;
+  }
+  constexpr int PB = 8;  // x fetched 8 positions at a time, one batch ahead
+  const size_t row0 = (size_t)b * T;
+  float cx[PB], nx[PB];
+#pragma unroll
+  for (int i = 0; i < PB; ++i) cx[i] = i < T ? xz[(row0 + i) * 2 * di + c] : 0.f;
+  for (int t0 = 0; t0 < T; t0 += PB) {
+#pragma unroll
+    for (int i = 0; i < PB; ++i) nx[i] = t0 + PB + i < T ? xz[(row0 + t0 + PB + i) * 2 * di + c] : 0.f;
+#pragma unroll
+    for (int i = 0; i < PB; ++i) {
+      if (t0 + i < T) {
+        const size_t row = row0 + t0 + i;
+        const float xt = cx[i];
+        const float o = conv_tap(w0, w1, w2, xt, k, bias);
+        u[row * di + c] = o;
+        __nv_bfloat16 h, l;
+        split_bf16(o, h, l);
+        uhl[row * di + c] = h;
+        uhl[plane + row * di + c] = l;
+        w0 = w1; w1 = w2; w2 = xt;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PB; ++i) cx[i] = nx[i];
   }
   s[0] = w0; s[di] = w1; s[2 * di] = w2;
 }
@@ -132,19 +151,32 @@ cudaError_t launch_conv(const float* xz, int di, float* cst, const float* cw, co
 //   h_n = exp(A_n dt) h_n + dt B_n u ;  y = sum_n h_n C_n + D u   (mamba_kernels.cu:271-361)
 //   out = y * silu(z)                               (mamba_kernels.cu:130-151)
 template <int R>
-__device__ __forceinline__ float scan_update(const float* __restrict__ dl, const float (&wdt)[R], float bdt,
+__device__ __forceinline__ float scan_update(const float4* __restrict__ dl4, const float (&wdt)[R], float bdt,
                                              const float (&na)[16], float (&h)[16], float uv, float z, float dsk) {
+  // dl4: the row's delta [dt_in(R) | B(16) | C(16)] as aligned float4 (128-bit shared loads)
   float acc = 0.f;
 #pragma unroll
-  for (int k = 0; k < R; ++k) acc = __fmaf_rn(dl[k], wdt[k], acc);
+  for (int k4 = 0; k4 < R / 4; ++k4) {
+    const float4 q = dl4[k4];
+    acc = __fmaf_rn(q.x, wdt[4 * k4 + 0], acc);
+    acc = __fmaf_rn(q.y, wdt[4 * k4 + 1], acc);
+    acc = __fmaf_rn(q.z, wdt[4 * k4 + 2], acc);
+    acc = __fmaf_rn(q.w, wdt[4 * k4 + 3], acc);
+  }
   const float dt = logf(__fadd_rn(1.0f, expf(__fadd_rn(acc, bdt))));
   float y = 0.f;
 #pragma unroll
-  for (int n = 0; n < 16; ++n) {
-    const float dA = __expf(__fmul_rn(na[n], dt));
-    const float dBu = __fmul_rn(__fmul_rn(dt, dl[R + n]), uv);
-    h[n] = __fmaf_rn(dA, h[n], dBu);
-    y = __fmaf_rn(h[n], dl[R + 16 + n], y);
+  for (int n4 = 0; n4 < 4; ++n4) {
+    const float4 b4 = dl4[R / 4 + n4], c4 = dl4[R / 4 + 4 + n4];
+    const float bb[4] = {b4.x, b4.y, b4.z, b4.w}, cc[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = 4 * n4 + j;
+      const float dA = __expf(__fmul_rn(na[n], dt));
+      const float dBu = __fmul_rn(__fmul_rn(dt, bb[j]), uv);
+      h[n] = __fmaf_rn(dA, h[n], dBu);
+      y = __fmaf_rn(h[n], cc[j], y);
+    }
   }
   y = __fmaf_rn(uv, dsk, y);
   return __fmul_rn(y, __fdiv_rn(z, __fadd_rn(1.0f, expf(-z))));
@@ -176,16 +208,39 @@ __global__ void __launch_bounds__(128) scan_tile_kernel(const float* __restrict_
 #pragma unroll
   for (int n = 0; n < 16; ++n) { na[n] = negA[(size_t)c * 16 + n]; h[n] = hp[(size_t)n * di]; }
   const float bdt = dtb[c], dsk = Dv[c];
-  size_t row = (size_t)b * T;
-  float un = u[row * di + c], zn = xz[row * 2 * di + di + c];
-  for (int tau = 0; tau < T; ++tau, ++row) {
-    const float uv = un, z = zn;
-    if (tau + 1 < T) { un = u[(row + 1) * di + c]; zn = xz[(row + 1) * 2 * di + di + c]; }
-    const float o = scan_update<R>(sdelta + tau * ld, wdt, bdt, na, h, uv, z, dsk);
-    __nv_bfloat16 hh, ll;
-    split_bf16(o, hh, ll);
-    yhl[row * di + c] = hh;
-    yhl[plane + row * di + c] = ll;
+  // u and z are fetched in batches of 8 positions, one batch ahead, so each
+  // thread keeps 16 loads in flight instead of waiting once per position.
+  constexpr int PB = 8;
+  const size_t row0 = (size_t)b * T;
+  float cu[PB], cz[PB], nu[PB], nz[PB];
+#pragma unroll
+  for (int i = 0; i < PB; ++i) {
+    const bool ok = i < T;
+    cu[i] = ok ? u[(row0 + i) * di + c] : 0.f;
+    cz[i] = ok ? xz[(row0 + i) * 2 * di + di + c] : 0.f;
+  }
+  for (int t0 = 0; t0 < T; t0 += PB) {
+#pragma unroll
+    for (int i = 0; i < PB; ++i) {
+      const bool ok = t0 + PB + i < T;
+      nu[i] = ok ? u[(row0 + t0 + PB + i) * di + c] : 0.f;
+      nz[i] = ok ? xz[(row0 + t0 + PB + i) * 2 * di + di + c] : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < PB; ++i) {
+      const int tau = t0 + i;
+      if (tau < T) {
+        const size_t row = row0 + tau;
+        const float o = scan_update<R>(reinterpret_cast<const float4*>(sdelta + tau * ld), wdt, bdt, na, h, cu[i],
+                                       cz[i], dsk);
+        __nv_bfloat16 hh, ll;
+        split_bf16(o, hh, ll);
+        yhl[row * di + c] = hh;
+        yhl[plane + row * di + c] = ll;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PB; ++i) { cu[i] = nu[i]; cz[i] = nz[i]; }
   }
 #pragma unroll
   for (int n = 0; n < 16; ++n) hp[(size_t)n * di] = h[n];
@@ -245,7 +300,7 @@ __global__ void __launch_bounds__(1024) scan_step_kernel(const float* __restrict
       float* hsm = reinterpret_cast<float*>(p);
       const float* usm = reinterpret_cast<const float*>(p + st_bytes);
       const float* zsm = usm + di;
-      const float* dl = reinterpret_cast<const float*>(p + st_bytes + 2 * uz_bytes);
+      const float4* dl = reinterpret_cast<const float4*>(p + st_bytes + 2 * uz_bytes);
       float h[16];
 #pragma unroll
       for (int n = 0; n < 16; ++n) h[n] = hsm[n * di + c];

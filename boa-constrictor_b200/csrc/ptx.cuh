@@ -185,6 +185,22 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Same for 64-byte rows (64-byte swizzle, layout 4, 8-row atoms of 512 B).
+template <int SWZ>
+__device__ __forceinline__ uint64_t umma_desc_swz(uint32_t smem_addr) {
+  if constexpr (SWZ == 128) {
+    return umma_desc_sw128(smem_addr);
+  } else {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;            // LBO (unused for swizzled K-major)
+    d |= (uint64_t)(512 >> 4) << 32;   // SBO = 8 rows * 64 B
+    d |= (uint64_t)1 << 46;            // version
+    d |= (uint64_t)4 << 61;            // SWIZZLE_64B
+    return d;
+  }
+}
+
 // Instruction descriptor, kind::f16: D=f32, A=B=bf16, both K-major, shape MxN.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
   return (1u << 4)                       // D format f32
