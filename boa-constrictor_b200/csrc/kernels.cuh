@@ -29,7 +29,8 @@ cudaError_t launch_conv(const float* xz, int di, float* conv_state, const float*
                         float* u, __nv_bfloat16* uhl, long long plane, int B, int T, cudaStream_t st);
 
 // selective scan with fused dt_proj + softplus + D skip + SiLU(z) gate.
-// delta [M][ld_delta] = [dt_in(r) | B(16) | C(16)]; ssm_state [B][16][di].
+// delta [M][ld_delta] = [dt_in(r) | B(16) | C(16)]; ssm_state [B][16][di];
+// negA holds -exp(A_log) * log2(e) per (channel, state).
 cudaError_t launch_scan(const float* delta, int ld_delta, int r, const float* dt_w, const float* dt_b,
                         const float* negA, const float* Dv, const float* u, const float* xz, int di,
                         float* ssm_state, __nv_bfloat16* yhl, long long plane, int B, int T, cudaStream_t st);

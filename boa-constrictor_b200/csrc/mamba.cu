@@ -98,17 +98,6 @@ __global__ void conv_kernel(const float* __restrict__ xz, int di, float* __restr
   float w0 = s[0], w1 = s[di], w2 = s[2 * di];
   const float4 k = reinterpret_cast<const float4*>(cw)[c];
   const float bias = cb[c];
-  if (T == 1) {  // decompress step: one position
-    const float xt = xz[(size_t)b * 2 * di + c];
-    const float o = conv_tap(w0, w1, w2, xt, k, bias);
-    u[(size_t)b * di + c] = o;
-    __nv_bfloat16 h, l;
-    split_bf16(o, h, l);
-    uhl[(size_t)b * di + c] = h;
-    uhl[plane + (size_t)b * di + c] = l;
-    s[0] = w1; s[di] = w2; s[2 * di] = xt;
-    return;
-  }
   constexpr int PB = 8;  // x fetched 8 positions at a time, one batch ahead
   const size_t row0 = (size_t)b * T;
   float cx[PB], nx[PB];
@@ -137,8 +126,40 @@ __global__ void conv_kernel(const float* __restrict__ xz, int di, float* __restr
   s[0] = w0; s[di] = w1; s[2 * di] = w2;
 }
 
+// Decompress step (T = 1): one thread per (chunk, 4 channels), 128-bit
+// accesses; the same conv_tap arithmetic as conv_kernel.
+__global__ void conv_step4_kernel(const float* __restrict__ xz, int di, float* __restrict__ cst,
+                                  const float* __restrict__ cw, const float* __restrict__ cb, float* __restrict__ u,
+                                  __nv_bfloat16* __restrict__ uhl, long long plane, int B) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int q = di / 4;
+  if (idx >= (long long)B * q) return;
+  const int b = (int)(idx / q), c = (int)(idx - (long long)b * q) * 4;
+  float4* s = reinterpret_cast<float4*>(cst + (size_t)b * 3 * di + c);
+  const float4 s0 = s[0], s1 = s[di / 4], s2 = s[di / 2];
+  const float4 x = *reinterpret_cast<const float4*>(xz + (size_t)b * 2 * di + c);
+  const float4 bias = *reinterpret_cast<const float4*>(cb + c);
+  const float4* k = reinterpret_cast<const float4*>(cw) + c;
+  float4 o;
+  o.x = conv_tap(s0.x, s1.x, s2.x, x.x, k[0], bias.x);
+  o.y = conv_tap(s0.y, s1.y, s2.y, x.y, k[1], bias.y);
+  o.z = conv_tap(s0.z, s1.z, s2.z, x.z, k[2], bias.z);
+  o.w = conv_tap(s0.w, s1.w, s2.w, x.w, k[3], bias.w);
+  *reinterpret_cast<float4*>(u + (size_t)b * di + c) = o;
+  __nv_bfloat16 h[4], l[4];
+  split_bf16(o.x, h[0], l[0]); split_bf16(o.y, h[1], l[1]); split_bf16(o.z, h[2], l[2]); split_bf16(o.w, h[3], l[3]);
+  *reinterpret_cast<uint2*>(uhl + (size_t)b * di + c) = *reinterpret_cast<uint2*>(h);
+  *reinterpret_cast<uint2*>(uhl + plane + (size_t)b * di + c) = *reinterpret_cast<uint2*>(l);
+  s[0] = s1; s[di / 4] = s2; s[di / 2] = x;
+}
+
 cudaError_t launch_conv(const float* xz, int di, float* cst, const float* cw, const float* cb, float* u,
                         __nv_bfloat16* uhl, long long plane, int B, int T, cudaStream_t st) {
+  if (T == 1 && di % 4 == 0) {
+    const long long n4 = (long long)B * (di / 4);
+    conv_step4_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(xz, di, cst, cw, cb, u, uhl, plane, B);
+    return cudaGetLastError();
+  }
   const long long n = (long long)B * di;
   conv_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(xz, di, cst, cw, cb, u, uhl, plane, B, T);
   return cudaGetLastError();
@@ -150,9 +171,16 @@ cudaError_t launch_conv(const float* xz, int di, float* cst, const float* cw, co
 //   dt = softplus(delta[:R] . Wdt[c] + b)          (dt_proj, inference_kernels.cu:372-390)
 //   h_n = exp(A_n dt) h_n + dt B_n u ;  y = sum_n h_n C_n + D u   (mamba_kernels.cu:271-361)
 //   out = y * silu(z)                               (mamba_kernels.cu:130-151)
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// na2 holds A * log2(e) (A = -exp(A_log)), so exp(A dt) = 2^(na2 dt).
 template <int R>
 __device__ __forceinline__ float scan_update(const float4* __restrict__ dl4, const float (&wdt)[R], float bdt,
-                                             const float (&na)[16], float (&h)[16], float uv, float z, float dsk) {
+                                             const float (&na2)[16], float (&h)[16], float uv, float z, float dsk) {
   // dl4: the row's delta [dt_in(R) | B(16) | C(16)] as aligned float4 (128-bit shared loads)
   float acc = 0.f;
 #pragma unroll
@@ -163,7 +191,8 @@ __device__ __forceinline__ float scan_update(const float4* __restrict__ dl4, con
     acc = __fmaf_rn(q.z, wdt[4 * k4 + 2], acc);
     acc = __fmaf_rn(q.w, wdt[4 * k4 + 3], acc);
   }
-  const float dt = logf(__fadd_rn(1.0f, expf(__fadd_rn(acc, bdt))));
+  const float dt = __logf(__fadd_rn(1.0f, __expf(__fadd_rn(acc, bdt))));  // softplus
+  const float dtu = __fmul_rn(dt, uv);
   float y = 0.f;
 #pragma unroll
   for (int n4 = 0; n4 < 4; ++n4) {
@@ -172,20 +201,19 @@ __device__ __forceinline__ float scan_update(const float4* __restrict__ dl4, con
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int n = 4 * n4 + j;
-      const float dA = __expf(__fmul_rn(na[n], dt));
-      const float dBu = __fmul_rn(__fmul_rn(dt, bb[j]), uv);
-      h[n] = __fmaf_rn(dA, h[n], dBu);
+      const float dA = ex2_ftz(__fmul_rn(na2[n], dt));
+      h[n] = __fmaf_rn(dA, h[n], __fmul_rn(bb[j], dtu));
       y = __fmaf_rn(h[n], cc[j], y);
     }
   }
   y = __fmaf_rn(uv, dsk, y);
-  return __fmul_rn(y, __fdiv_rn(z, __fadd_rn(1.0f, expf(-z))));
+  return __fmul_rn(y, __fdividef(z, __fadd_rn(1.0f, __expf(-z))));  // y * silu(z)
 }
 
 // Compress form: thread per (chunk, channel), h[16] in registers across the T
 // rows of the tile; the chunk's delta rows are staged in shared memory.
 template <int R>
-__global__ void __launch_bounds__(128) scan_tile_kernel(const float* __restrict__ delta, int ld, const float* __restrict__ dtw,
+__global__ void __launch_bounds__(128, 5) scan_tile_kernel(const float* __restrict__ delta, int ld, const float* __restrict__ dtw,
                                                         const float* __restrict__ dtb, const float* __restrict__ negA,
                                                         const float* __restrict__ Dv, const float* __restrict__ u,
                                                         const float* __restrict__ xz, int di, float* __restrict__ hs,
@@ -208,9 +236,9 @@ __global__ void __launch_bounds__(128) scan_tile_kernel(const float* __restrict_
 #pragma unroll
   for (int n = 0; n < 16; ++n) { na[n] = negA[(size_t)c * 16 + n]; h[n] = hp[(size_t)n * di]; }
   const float bdt = dtb[c], dsk = Dv[c];
-  // u and z are fetched in batches of 8 positions, one batch ahead, so each
-  // thread keeps 16 loads in flight instead of waiting once per position.
-  constexpr int PB = 8;
+  // u and z are fetched in batches of 4 positions, one batch ahead, so each
+  // thread keeps 8 loads in flight instead of waiting once per position.
+  constexpr int PB = 4;
   const size_t row0 = (size_t)b * T;
   float cu[PB], cz[PB], nu[PB], nz[PB];
 #pragma unroll

@@ -15,7 +15,7 @@ __device__ __forceinline__ float conv_tap(float w0, float w1, float w2, float x,
   v = __fadd_rn(v, __fmul_rn(w1, k.y));
   v = __fadd_rn(v, __fmul_rn(w2, k.z));
   v = __fadd_rn(v, __fmul_rn(x, k.w));
-  return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+  return __fdividef(v, __fadd_rn(1.0f, __expf(-v)));  // v * sigmoid(v)
 }
 
 }  // namespace boa

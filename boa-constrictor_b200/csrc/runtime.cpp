@@ -464,7 +464,8 @@ int boa_model_load(const char* path, int backbone, int d, int nl, int device, bo
       x.dt_w = addf(R.vec((size_t)di * r));
       x.dt_b = addf(R.vec(di));
       std::vector<float> alog = R.vec((size_t)di * 16);
-      for (auto& a : alog) a = -std::exp(a);
+      // stored as A * log2(e) with A = -exp(A_log): the scan evaluates exp(A dt) as 2^(na2 dt)
+      for (auto& a : alog) a = -std::exp(a) * 1.44269504088896340736f;
       x.negA = addf(std::move(alog));
       x.Dv = addf(R.vec(di));
       x.out = addh(make_hl(R.vec((size_t)d * di), d, di, d));
