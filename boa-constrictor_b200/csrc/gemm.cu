@@ -560,8 +560,10 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           if constexpr (MODE == EPI_RES_LN) {
             tile_put_row(wb, lane, v);
             tile_store_f32(wb, lane, args.res + (size_t)wrow0 * BN + c, BN, nrows);
+            tmem_st16(trow + c, v);  // keep x in the (consumed) accumulator for pass 2
           }
         }
+        if constexpr (MODE == EPI_RES_LN) tmem_st_wait();
         red[(r_local * 4 + part) * 2 + 0] = sum;
         red[(r_local * 4 + part) * 2 + 1] = sq;
         named_bar_sync(1, kEpiThreads);
@@ -579,9 +581,7 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           float v[16];
           tmem_ld16(trow + c, v);
           if constexpr (MODE == EPI_RES_LN) {
-            // x = acc + bias + residual was stored in pass 1; read it back
-            tile_load_f32(wb, lane, args.res + (size_t)wrow0 * BN + c, BN, nrows);
-            tile_get_row(wb, lane, v);
+            // v already holds x = acc + bias + residual (written back to TMEM in pass 1)
           } else {
             float bb[16];
             load_bias16(args.bias + c, bb);
