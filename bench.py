@@ -96,6 +96,12 @@ def algorithmic_per_launch(cls, B, T, d, L):
     return None, 0.0
 
 
+# DRAM bytes (read + write) of one launch from `ncu --set full`, recorded in
+# profiles/ncu_launches_small_roundtrip.md, per chunk of the batch (the
+# kernel's traffic scales with the number of chunks): decompress-step scan.
+NCU_TRAFFIC_PER_CHUNK = {("scan", "decode"): (608.086784e6 + 523.836672e6) / 16384}
+
+
 # --------------------------------------------------------------------------- clocks
 class Clocks:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -378,7 +384,9 @@ def main():
             "decompress_MBps": total / MiB / (dec_ms * 1e-3),
             "bits_per_byte": bpb, "roundtrip_ok": ok and e2e_ok,
             "roofline": {"kernel": dom, "phase": phase, "bound": bound, "achieved": achieved, "peak": peak,
-                         "unit": unit, "frac": achieved / peak, "traffic": None,
+                         "unit": unit, "frac": achieved / peak,
+                         "traffic": (NCU_TRAFFIC_PER_CHUNK[(dom, "decode")] * C
+                                     if in_decode and (dom, "decode") in NCU_TRAFFIC_PER_CHUNK else None),
                          "peak_source": f"{peak_kind} ({'bf16 sustained' if bound == 'tensor' else 'HBM copy'})"},
             "kernels": kern,
             "cpu_baseline": cpu,

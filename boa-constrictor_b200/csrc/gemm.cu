@@ -390,9 +390,16 @@ struct PCfg {
   static constexpr int kRed = kBM * 4 * 2 * 4;
   static constexpr int kBudget = 225 * 1024 - 1024 - 256 - kRed - kEpiBuf;
   static constexpr int kStages = kBudget / kStageBytes > 8 ? 8 : kBudget / kStageBytes;
-  static constexpr int kAccCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
-  static constexpr int kTmemCols = 2 * kAccCols;
+  // N > 256 (LayerNorm over d = 512): 256-wide MMAs side by side in one
+  // 512-column accumulator, which then cannot be double-buffered.
+  static constexpr int kMmaN = BN > 256 ? 256 : BN;
+  static constexpr int kNSub = BN / kMmaN;
+  static constexpr int kBoxRows = kMmaN;
+  static constexpr int kAccCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : BN <= 256 ? 256 : 512;
+  static constexpr int kNumAcc = 2 * kAccCols <= 512 ? 2 : 1;
+  static constexpr int kTmemCols = kNumAcc * kAccCols;
   static constexpr int kSmem = kStages * kStageBytes + 1024 + 256 + kRed + kEpiBuf;
+  static_assert(kStages >= 2, "pipeline needs at least two stages");
 };
 
 template <int BN, int MODE>
@@ -443,19 +450,23 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           const int k0 = kb * Cfg::kBK;
           tma_load_3d(st, &tmA, &full[s], k0, m0, 0);
           tma_load_3d(st + Cfg::kABytes, &tmA, &full[s], k0, m0, 1);
-          tma_load_3d(st + 2 * Cfg::kABytes, &tmW, &full[s], k0, n0, 0);
-          tma_load_3d(st + 2 * Cfg::kABytes + Cfg::kBBytes, &tmW, &full[s], k0, n0, 1);
+#pragma unroll
+          for (int sub = 0; sub < Cfg::kNSub; ++sub) {
+            const int off = sub * Cfg::kBoxRows * Cfg::kBK * 2;
+            tma_load_3d(st + 2 * Cfg::kABytes + off, &tmW, &full[s], k0, n0 + sub * Cfg::kBoxRows, 0);
+            tma_load_3d(st + 2 * Cfg::kABytes + Cfg::kBBytes + off, &tmW, &full[s], k0, n0 + sub * Cfg::kBoxRows, 1);
+          }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
+      constexpr uint32_t idesc = umma_idesc_bf16(kBM, Cfg::kMmaN);
       int g = 0, it = 0;
       for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
-        const int a = it & 1;
+        const int a = it % Cfg::kNumAcc, use = it / Cfg::kNumAcc;
         const uint32_t acc = tmem + (uint32_t)(a * Cfg::kAccCols);
-        if (it >= 2 && !mbar_wait(&acc_empty[a], ((it >> 1) - 1) & 1)) { *abort_flag = 1; }
+        if (it >= Cfg::kNumAcc && !mbar_wait(&acc_empty[a], (use - 1) & 1)) { *abort_flag = 1; }
         if (*abort_flag) { umma_commit(&acc_full[a]); break; }
         tc_fence_after();
         for (int kb = 0; kb < nkb; ++kb, ++g) {
@@ -470,9 +481,14 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 #pragma unroll
           for (int kk = 0; kk < Cfg::kBK / 16; ++kk) {
             const uint64_t adv = (uint64_t)(kk * 32 >> 4);
-            umma_bf16(acc, dAh + adv, dWh + adv, idesc, (kb | kk) != 0);
-            umma_bf16(acc, dAh + adv, dWl + adv, idesc, 1u);
-            umma_bf16(acc, dAl + adv, dWh + adv, idesc, 1u);
+#pragma unroll
+            for (int sub = 0; sub < Cfg::kNSub; ++sub) {
+              const uint64_t bo = (uint64_t)((sub * Cfg::kBoxRows * Cfg::kBK * 2) >> 4);
+              const uint32_t d = acc + (uint32_t)(sub * Cfg::kMmaN);
+              umma_bf16(d, dAh + adv, dWh + bo + adv, idesc, (kb | kk) != 0);
+              umma_bf16(d, dAh + adv, dWl + bo + adv, idesc, 1u);
+              umma_bf16(d, dAl + adv, dWh + bo + adv, idesc, 1u);
+            }
           }
           umma_commit(&empty[s]);
         }
@@ -488,11 +504,11 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     constexpr int kChunks = BN / 16;
     int it = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
-      const int a = it & 1;
+      const int a = it % Cfg::kNumAcc, use = it / Cfg::kNumAcc;
       const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
       // only the barrier outcome decides (uniform across the epilogue warps,
       // which then meet at named barriers)
-      const bool ok = mbar_wait(&acc_full[a], (it >> 1) & 1);
+      const bool ok = mbar_wait(&acc_full[a], use & 1);
       tc_fence_after();
       if (!ok) break;
 #ifdef BOA_EPI_STUB  // experiment builds only: drain the accumulator without an epilogue
@@ -716,12 +732,15 @@ cudaError_t gemm_prepare_device() {
   if ((e = set_attrs<48>()) != cudaSuccess) return e;
   if ((e = set_attrs<64>()) != cudaSuccess) return e;
   if ((e = set_attrs<128>()) != cudaSuccess) return e;
-  return set_attrs<256>();
+  if ((e = set_attrs<256>()) != cudaSuccess) return e;
+  if ((e = set_attr_t<512, EPI_LN_SPLIT>()) != cudaSuccess) return e;
+  return set_attr_t<512, EPI_RES_LN>();
 }
 
 // CTA tile width: a full row for the row-wise epilogues (LayerNorm, coder),
 // 256 for wide outputs, else the (padded) width itself.
 static int pick_bn(int mode, int N) {
+  if ((mode == EPI_LN_SPLIT || mode == EPI_RES_LN) && N == 512) return 512;
   if (mode == EPI_LN_SPLIT || mode == EPI_RES_LN || mode >= EPI_LOGITS) return N;
   if (N % 256 == 0) return 256;
   return N;
@@ -731,17 +750,21 @@ cudaError_t gemm_launch(int mode, const __nv_bfloat16* A, long long a_plane, int
                         const __nv_bfloat16* W, long long w_plane, const GemmArgs& args, cudaStream_t stream) {
   if (args.K % 16 != 0 || args.K <= 0 || args.M <= 0) return cudaErrorInvalidValue;
   const int BN = pick_bn(mode, args.N);
-  if (BN != 48 && BN != 64 && BN != 128 && BN != 256) return cudaErrorInvalidValue;
+  if (BN != 48 && BN != 64 && BN != 128 && BN != 256 && BN != 512) return cudaErrorInvalidValue;
   if (mode >= EPI_LOGITS && BN != 256) return cudaErrorInvalidValue;
   // persistent row-parallel modes with BN >= 128 use K-blocks of 32
   const int box_k = (mode <= EPI_RES_LN && BN >= 128) ? 32 : kBK;
   CUtensorMap ta, tw;
   if (!make_plane_map(&ta, A, args.K, args.M, a_plane, kBM, box_k)) return cudaErrorInvalidValue;
-  if (!make_plane_map(&tw, W, args.K, args.N, w_plane, BN, box_k)) return cudaErrorInvalidValue;
+  if (!make_plane_map(&tw, W, args.K, args.N, w_plane, BN > 256 ? 256 : BN, box_k)) return cudaErrorInvalidValue;
   switch (BN) {
     case 48: return dispatch<48>(mode, ta, tw, args, stream);
     case 64: return dispatch<64>(mode, ta, tw, args, stream);
     case 128: return dispatch<128>(mode, ta, tw, args, stream);
+    case 512:
+      if (mode == EPI_LN_SPLIT) return launch_t<512, EPI_LN_SPLIT>(ta, tw, args, stream);
+      if (mode == EPI_RES_LN) return launch_t<512, EPI_RES_LN>(ta, tw, args, stream);
+      return cudaErrorInvalidValue;
     default: return dispatch<256>(mode, ta, tw, args, stream);
   }
 }

@@ -406,8 +406,8 @@ int boa_model_load(const char* path, int backbone, int d, int nl, int device, bo
   *out = nullptr;
   if (backbone != BOA_BACKBONE_MAMBA && backbone != BOA_BACKBONE_MINGRU)
     return fail(nullptr, BOA_E_INVALID, "backbone must be mamba (0) or mingru (3)");
-  if (!(d == 64 || d == 128 || d == 256) || nl <= 0 || nl > 256)
-    return fail(nullptr, BOA_E_INVALID, "d_model must be 64, 128 or 256 and n_layers in 1..256");
+  if (!(d == 64 || d == 128 || d == 256 || d == 512) || nl <= 0 || nl > 256)
+    return fail(nullptr, BOA_E_INVALID, "d_model must be 64, 128, 256 or 512 and n_layers in 1..256");
   FileReader R;
   {
     FILE* f = path ? std::fopen(path, "rb") : nullptr;

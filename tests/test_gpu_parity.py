@@ -201,3 +201,17 @@ def test_state_reset_after_a_larger_batch(boa, m64):
     m64.compress(big, 300)
     b = m64.compress(small, 300)
     assert all(np.array_equal(x, y) for x, y in zip(a, b))
+
+
+def test_d512_logits_forms_and_roundtrip(boa, oracle, weights):
+    """configs[4] geometry (d_model 512: d_inner 1024, dt_rank 32, 512-wide
+    LayerNorm epilogues) on a 2-layer model."""
+    p = weights("mamba", 512, 2, 3)
+    m = boa.Model(p, "mamba", 512, 2)
+    tok = np.random.default_rng(13).integers(0, 256, (2, 24), dtype=np.uint8)
+    ref = oracle.OracleModel(p, 0, 512, 2).logits(tok, 0)
+    lg = m.logits(tok, 0)
+    assert np.abs(lg - ref).max() <= LOGIT_RTOL * np.abs(ref).max()
+    assert np.array_equal(lg, m.logits(tok, 1))
+    data = boa.synth.particle_stream(3 * 700 + 5, 4)
+    _roundtrip(boa, m, data, 700)
