@@ -21,6 +21,7 @@ import subprocess
 import numpy as np
 
 from . import synth  # noqa: F401  (seeded inputs for tests and bench)
+from . import sharding  # noqa: F401  (multi-rank chunk sharding)
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libboa_b200.so")
