@@ -64,6 +64,7 @@ SIGNATURES = {
     "boa_set_temperature": (C.c_int, [C.c_void_p, C.c_float]),
     "boa_set_stream": (C.c_int, [C.c_void_p, C.c_void_p]),
     "boa_set_batch": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "boa_set_warm_start": (C.c_int, [C.c_void_p, C.c_uint32]),
     "boa_stream_capacity_words": (C.c_uint32, [C.c_uint32]),
     "boa_compress_chunks": (C.c_int, [C.c_void_p, _u8p, C.c_size_t, C.c_uint32, C.c_uint32, C.c_uint32, _u8p,
                                       _u32p, C.c_size_t, _u32p, _u64p]),
@@ -148,6 +149,9 @@ class Model:
 
     def set_batch(self, chunks: int = 0, tile: int = 0):
         _check(lib().boa_set_batch(self.h, chunks, tile), self.h)
+
+    def set_warm_start(self, interleave_batch: int):
+        _check(lib().boa_set_warm_start(self.h, interleave_batch), self.h)
 
     def set_stream(self, stream_ptr: int | None):
         _check(lib().boa_set_stream(self.h, C.c_void_p(stream_ptr or 0)), self.h)
@@ -254,7 +258,8 @@ class Model:
 
 
 # -------------------------------------------------------------------- container
-def boa2_build(total_size: int, chunk_len: int, first_bytes, sizes_words, payload_words) -> bytes:
+def boa2_build(total_size: int, chunk_len: int, first_bytes, sizes_words, payload_words, warm_start: int = 0) -> bytes:
+    """warm_start = interleave batch W of a warm-start container (flags bit0), 0 = off."""
     n = len(sizes_words)
     last = total_size - (n - 1) * chunk_len if n > 1 else total_size
     fb = np.ascontiguousarray(first_bytes, np.uint8)
@@ -267,11 +272,12 @@ def boa2_build(total_size: int, chunk_len: int, first_bytes, sizes_words, payloa
     if sb.size == 0:
         sb = np.zeros(1, np.uint64)
     ln = C.c_size_t()
-    _check(lib().boa_boa2_build(total_size, chunk_len, n, last, 0, 0, _p(fb, _u8p), _p(sb, _u64p), _p(pay, _u8p),
-                                None, 0, C.byref(ln)))
+    flags = 1 if warm_start else 0
+    _check(lib().boa_boa2_build(total_size, chunk_len, n, last, flags, warm_start, _p(fb, _u8p), _p(sb, _u64p),
+                                _p(pay, _u8p), None, 0, C.byref(ln)))
     buf = np.zeros(ln.value, np.uint8)
-    _check(lib().boa_boa2_build(total_size, chunk_len, n, last, 0, 0, _p(fb, _u8p), _p(sb, _u64p), _p(pay, _u8p),
-                                _p(buf, _u8p), buf.size, C.byref(ln)))
+    _check(lib().boa_boa2_build(total_size, chunk_len, n, last, flags, warm_start, _p(fb, _u8p), _p(sb, _u64p),
+                                _p(pay, _u8p), _p(buf, _u8p), buf.size, C.byref(ln)))
     return buf.tobytes()
 
 

@@ -11,6 +11,7 @@
 // ranges, one host thread and one library handle per GPU); the container is
 // the same BOA2 file either way.  --warm-start is not supported yet and is
 // rejected rather than silently ignored.
+#include <algorithm>
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
@@ -30,7 +31,7 @@ struct Opts {
   int d_model = 256, n_layers = 1, gpu_batch = 0, max_chunks = -1, tile = 0, gpus = 1;
   size_t chunk = 4096;
   float temperature = 1.0f;
-  bool timings = false;
+  bool timings = false, warm = false;
 };
 
 bool read_file(const std::string& p, std::vector<uint8_t>& v) {
@@ -77,6 +78,12 @@ int do_compress(const Opts& o) {
   const uint32_t last = (uint32_t)(n_chunks > 1 ? processed - (size_t)(n_chunks - 1) * o.chunk : processed);
   std::cout << "Compressing " << processed << " bytes in " << n_chunks << " chunks on " << o.gpus << " GPU(s)..."
             << std::endl;
+  uint32_t warm_w = 0;
+  if (o.warm) {
+    if (o.gpus != 1) { std::cerr << "Error: --warm-start needs --gpus 1\n"; return 1; }
+    warm_w = (uint32_t)std::min<uint64_t>(o.gpu_batch > 0 ? o.gpu_batch : 64, n_chunks);  // boa.cpp:310-311
+    std::cout << "Warm start: " << warm_w << " lanes" << std::endl;
+  }
   std::vector<uint8_t> first(n_chunks);
   std::vector<uint32_t> sizes(n_chunks);
   const auto sh = shards(n_chunks, o.gpus);
@@ -88,6 +95,7 @@ int do_compress(const Opts& o) {
     th.emplace_back([&, g]() {
       boa_model* h = nullptr;
       if ((rcs[g] = open_model(o, (int)g, &h))) return;
+      if (warm_w) boa_set_warm_start(h, warm_w);
       const Shard s = sh[g];
       size_t cap = (size_t)s.n * boa_stream_capacity_words((uint32_t)o.chunk);
       pay[g].resize(cap);
@@ -107,11 +115,12 @@ int do_compress(const Opts& o) {
   std::vector<uint64_t> sb(n_chunks);
   for (uint32_t i = 0; i < n_chunks; ++i) sb[i] = (uint64_t)sizes[i] * 4;
   size_t len = 0;
-  boa_boa2_build(processed, (uint32_t)o.chunk, n_chunks, last, 0, 0, first.data(), sb.data(), payload.data(), nullptr,
-                 0, &len);
+  const uint32_t flags = warm_w ? 1u : 0u;
+  boa_boa2_build(processed, (uint32_t)o.chunk, n_chunks, last, flags, warm_w, first.data(), sb.data(), payload.data(),
+                 nullptr, 0, &len);
   std::vector<uint8_t> blob(len);
-  if (boa_boa2_build(processed, (uint32_t)o.chunk, n_chunks, last, 0, 0, first.data(), sb.data(), payload.data(),
-                     blob.data(), blob.size(), &len)) {
+  if (boa_boa2_build(processed, (uint32_t)o.chunk, n_chunks, last, flags, warm_w, first.data(), sb.data(),
+                     payload.data(), blob.data(), blob.size(), &len)) {
     std::cerr << "Error: container build failed\n";
     return 1;
   }
@@ -131,7 +140,9 @@ int do_decompress(const Opts& o) {
     std::cerr << "Error: not a valid BOA2 container\n";
     return 1;
   }
-  if (I.flags & 1u) { std::cerr << "Error: warm-start containers are not supported yet\n"; return 1; }
+  const uint32_t warm_w = (I.flags & 1u) ? I.interleave_batch : 0u;  // boa.cpp:608-610
+  if (warm_w && o.gpus != 1) { std::cerr << "Error: warm-start containers decode on one GPU\n"; return 1; }
+  if ((I.flags & 1u) && warm_w == 0) { std::cerr << "Error: warm-start container without its batch\n"; return 1; }
   const uint32_t n = I.n_chunks;
   std::vector<uint8_t> first(n);
   std::vector<uint64_t> off(n), len(n);
@@ -160,6 +171,7 @@ int do_decompress(const Opts& o) {
     th.emplace_back([&, g]() {
       boa_model* h = nullptr;
       if ((rcs[g] = open_model(o, (int)g, &h))) return;
+      if (warm_w) boa_set_warm_start(h, warm_w);
       const Shard s = sh[g];
       rcs[g] = boa_decompress_chunks(h, words.data() + woff[s.c0], sizes.data() + s.c0, first.data() + s.c0,
                                      lens.data() + s.c0, I.chunk_len, s.n, out.data() + (size_t)s.c0 * I.chunk_len);
@@ -204,7 +216,7 @@ int main(int argc, char** argv) {
       else if (s == "--gpus") o.gpus = std::stoi(next("--gpus"));
       else if (s == "--show-timings") o.timings = true;
       else if (s == "--no-graph" || s == "--gpu") continue;
-      else if (s == "--warm-start") { std::cerr << "Error: --warm-start is not supported yet\n"; return 1; }
+      else if (s == "--warm-start") o.warm = true;
       else if (s == "--measure-energy") { std::cerr << "Warning: --measure-energy is not supported; ignored.\n"; }
       else if (s.rfind("--", 0) == 0) std::cerr << "Warning: Unknown flag '" << s << "' ignored.\n";
       else pos.push_back(s);

@@ -250,7 +250,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           SmemRow src{srow};
           if constexpr (MODE == EPI_HEAD_ENC) {
             const int b = row / args.T, tau = row - b * args.T;
-            const long long base = (long long)b * args.chunk_len;
+            const long long base = (long long)b * (args.stride ? args.stride : args.chunk_len);
             const long long rem = args.n_bytes - base;
             const int len = (int)(rem < args.chunk_len ? rem : args.chunk_len);
             const int p = args.t0 + tau;
@@ -265,9 +265,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           } else {
             const int b = row;
             const int t = *args.d_t;
-            const long long base = (long long)b * args.chunk_len;
-            const long long rem = args.n_bytes - base;
-            const int len = (int)(rem < args.chunk_len ? rem : args.chunk_len);
+            const long long base = args.lane_base[b];
+            const int len = args.lane_len[b];
             if (t < len) {
               DecState st = args.dstates[b];
               const uint32_t* in = args.payload + args.offsets[b];

@@ -41,10 +41,13 @@ struct GemmArgs {
   int chunk_len;
   int t0, T;              // compress tile: rows are (b, tau), position t0 + tau
   uint2* lf;              // compress: [M] (low, high) per row
+  long long stride;       // compress: bytes between lanes' chunks (0 = chunk_len)
   const int* d_t;         // decompress: device step counter
+  const long long* lane_base;  // decompress: each lane's chunk offset in out_bytes
+  const int* lane_len;         // decompress: each lane's chunk length
   DecState* dstates;      // decompress: one decoder per chunk
   const uint32_t* payload;
-  const unsigned long long* offsets;  // word offset of each chunk's stream
+  const unsigned long long* offsets;  // word offset of each lane's stream
 };
 
 struct PlaneMap;  // opaque TMA descriptor holder (host)

@@ -12,10 +12,14 @@ namespace boa {
 // Where each row's input token comes from.
 struct TokenSrc {
   int mode;               // 0: tokens[row]; 1: compress tile; 2: decompress step
-  const uint8_t* bytes;   // mode 0: [M]; mode 1: batch input; mode 2: batch output
-  long long n_bytes;      // bytes from the batch's first chunk to the stream end
+  const uint8_t* bytes;   // mode 0: [M]; mode 1: lane 0's chunk; mode 2: output stream
+  long long n_bytes;      // mode 1: bytes from lane 0's chunk to the stream end
   int chunk_len, t0, T;   // mode 1
   const int* d_t;         // mode 2: current step; the token is byte t-1
+  long long stride;       // mode 1: bytes between consecutive lanes' chunks (0 = chunk_len;
+                          //         S * chunk_len for interleaved warm-start lanes)
+  const long long* lane_base;  // mode 2: byte offset of each lane's chunk in `bytes`
+  const int* lane_len;         // mode 2: length of each lane's chunk
 };
 
 // x[row] = E[token]; xn = split(LN(x; w, b))   (rows = M, width d)
@@ -48,22 +52,34 @@ cudaError_t launch_add_ln(float* x, const float* y, int d, __nv_bfloat16* xn, lo
 cudaError_t launch_rms_split(const float* x, int d, const float* w, __nv_bfloat16* xn, long long plane, int M,
                              cudaStream_t st);
 
-// compress: encode one tile of (low, high) per chunk; lf [B][T]
+// compress: encode one tile of (low, high) per lane; lf [B][T]; lane b's
+// chunk starts b * stride bytes after lane 0's
 cudaError_t launch_encode_tile(const uint2* lf, EncState* es, uint32_t* pitch_buf, int pitch_words, int B,
-                               int T, int t0, long long n_bytes, int chunk_len, cudaStream_t st);
+                               int T, int t0, long long n_bytes, int chunk_len, long long stride, cudaStream_t st);
 cudaError_t launch_enc_init(EncState* es, int B, cudaStream_t st);
 cudaError_t launch_enc_finish(EncState* es, uint32_t* pitch_buf, int pitch_words, uint32_t* sizes, int B,
                               cudaStream_t st);
-// exclusive scan of sizes -> offsets (one block); total in offsets[B]
+// exclusive scan of sizes -> offsets (one block), continuing from offsets[0];
+// total in offsets[B]
 cudaError_t launch_offsets(const uint32_t* sizes, unsigned long long* offsets, int B, cudaStream_t st);
 cudaError_t launch_compact(const uint32_t* pitch_buf, int pitch_words, const uint32_t* sizes,
                            const unsigned long long* offsets, uint32_t* payload, int B, cudaStream_t st);
-cudaError_t launch_first_bytes(const uint8_t* data, long long n_bytes, int chunk_len, uint8_t* first, int B,
-                               cudaStream_t st);
-// decompress
-cudaError_t launch_dec_init(DecState* ds, const uint32_t* payload, const unsigned long long* offsets,
-                            const uint32_t* sizes, const uint8_t* first, uint8_t* out, long long n_bytes,
-                            int chunk_len, int B, cudaStream_t st);
+cudaError_t launch_first_bytes(const uint8_t* data, long long n_bytes, int chunk_len, long long stride, uint8_t* first,
+                               int B, cudaStream_t st);
+// compress, interleaved lanes: lane b's results -> chunk c = iter + b * S
+// (sizes, first bytes, and its stream copied into per-chunk slots)
+cudaError_t launch_lanes_scatter(const uint32_t* pitch_buf, int pitch_words, const uint32_t* lane_sizes,
+                                 const uint8_t* lane_first, uint32_t* slots, uint32_t* sizes, uint8_t* first, int iter,
+                                 int S, int B, cudaStream_t st);
+// decompress: per-lane view of chunks c = c0 + b * S (stream offset, size,
+// first byte, output offset and length)
+cudaError_t launch_lanes_gather(const unsigned long long* offsets, const uint32_t* sizes, const uint8_t* first,
+                                long long n_bytes, int chunk_len, int c0, int S, int B, unsigned long long* lane_off,
+                                uint32_t* lane_size, uint8_t* lane_first, long long* lane_base, int* lane_len,
+                                cudaStream_t st);
+cudaError_t launch_dec_init(DecState* ds, const uint32_t* payload, const unsigned long long* lane_off,
+                            const uint32_t* lane_size, const uint8_t* lane_first, uint8_t* out,
+                            const long long* lane_base, const int* lane_len, int B, cudaStream_t st);
 cudaError_t launch_set_counter(int* d_t, int value, cudaStream_t st);
 cudaError_t launch_increment(int* d_t, cudaStream_t st);
 

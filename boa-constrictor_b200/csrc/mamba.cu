@@ -16,8 +16,8 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-__device__ __forceinline__ int chunk_len_of(long long n_bytes, int chunk_len, int b) {
-  const long long rem = n_bytes - (long long)b * chunk_len;
+__device__ __forceinline__ int chunk_len_of(long long n_bytes, int chunk_len, int b, long long stride = 0) {
+  const long long rem = n_bytes - (long long)b * (stride ? stride : chunk_len);
   return (int)(rem < chunk_len ? (rem > 0 ? rem : 0) : chunk_len);
 }
 
@@ -38,11 +38,12 @@ __global__ void embed_ln_kernel(TokenSrc src, const float* __restrict__ emb, flo
   } else if (src.mode == 1) {
     const int b = row / src.T, tau = row - b * src.T;
     const int p = src.t0 + tau;
-    if (p < chunk_len_of(src.n_bytes, src.chunk_len, b)) tok = src.bytes[(long long)b * src.chunk_len + p];
+    const long long stride = src.stride ? src.stride : src.chunk_len;
+    if (p < chunk_len_of(src.n_bytes, src.chunk_len, b, stride)) tok = src.bytes[(long long)b * stride + p];
   } else {
     const int b = row;
     const int p = *src.d_t - 1;
-    if (p >= 0 && p < chunk_len_of(src.n_bytes, src.chunk_len, b)) tok = src.bytes[(long long)b * src.chunk_len + p];
+    if (p >= 0 && p < src.lane_len[b]) tok = src.bytes[src.lane_base[b] + p];
   }
   float v[V];
   float s = 0.f, sq = 0.f;
@@ -512,10 +513,10 @@ cudaError_t launch_enc_init(EncState* es, int B, cudaStream_t st) {
 // (encode loop of range_coder_kernels.cu:856-966 with the CDF already reduced
 // to (low, high) by the head epilogue).
 __global__ void encode_tile_kernel(const uint2* __restrict__ lf, EncState* es, uint32_t* pitch_buf, int pitch,
-                                   int B, int T, int t0, long long n_bytes, int chunk_len) {
+                                   int B, int T, int t0, long long n_bytes, int chunk_len, long long stride) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
-  const int len = chunk_len_of(n_bytes, chunk_len, b);
+  const int len = chunk_len_of(n_bytes, chunk_len, b, stride);
   int n = len - 1 - t0;
   if (n <= 0) return;
   if (n > T) n = T;
@@ -529,8 +530,8 @@ __global__ void encode_tile_kernel(const uint2* __restrict__ lf, EncState* es, u
   es[b] = s;
 }
 cudaError_t launch_encode_tile(const uint2* lf, EncState* es, uint32_t* pitch_buf, int pitch, int B, int T, int t0,
-                               long long n_bytes, int chunk_len, cudaStream_t st) {
-  encode_tile_kernel<<<(B + 127) / 128, 128, 0, st>>>(lf, es, pitch_buf, pitch, B, T, t0, n_bytes, chunk_len);
+                               long long n_bytes, int chunk_len, long long stride, cudaStream_t st) {
+  encode_tile_kernel<<<(B + 127) / 128, 128, 0, st>>>(lf, es, pitch_buf, pitch, B, T, t0, n_bytes, chunk_len, stride);
   return cudaGetLastError();
 }
 
@@ -587,37 +588,83 @@ cudaError_t launch_compact(const uint32_t* pitch_buf, int pitch, const uint32_t*
   return cudaGetLastError();
 }
 
-__global__ void first_bytes_kernel(const uint8_t* data, long long n_bytes, int chunk_len, uint8_t* first, int B) {
+__global__ void first_bytes_kernel(const uint8_t* data, long long n_bytes, int chunk_len, long long stride,
+                                   uint8_t* first, int B) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
-  first[b] = chunk_len_of(n_bytes, chunk_len, b) > 0 ? data[(long long)b * chunk_len] : 0;
+  if (!stride) stride = chunk_len;
+  first[b] = chunk_len_of(n_bytes, chunk_len, b, stride) > 0 ? data[(long long)b * stride] : 0;
 }
-cudaError_t launch_first_bytes(const uint8_t* data, long long n_bytes, int chunk_len, uint8_t* first, int B,
-                               cudaStream_t st) {
-  first_bytes_kernel<<<(B + 255) / 256, 256, 0, st>>>(data, n_bytes, chunk_len, first, B);
+cudaError_t launch_first_bytes(const uint8_t* data, long long n_bytes, int chunk_len, long long stride, uint8_t* first,
+                               int B, cudaStream_t st) {
+  first_bytes_kernel<<<(B + 255) / 256, 256, 0, st>>>(data, n_bytes, chunk_len, stride, first, B);
+  return cudaGetLastError();
+}
+
+// interleaved (warm-start) lanes: lane b of iteration `iter` coded chunk
+// iter + b * S (boa.cpp:395-406, :414); move its results to chunk order
+__global__ void lanes_scatter_kernel(const uint32_t* __restrict__ pitch_buf, int pitch,
+                                     const uint32_t* __restrict__ lane_sizes, const uint8_t* __restrict__ lane_first,
+                                     uint32_t* __restrict__ slots, uint32_t* __restrict__ sizes,
+                                     uint8_t* __restrict__ first, int iter, int S) {
+  const int b = blockIdx.x;
+  const size_t c = (size_t)iter + (size_t)b * S;
+  const uint32_t n = lane_sizes[b];
+  if (threadIdx.x == 0) { sizes[c] = n; first[c] = lane_first[b]; }
+  const uint32_t* src = pitch_buf + (size_t)b * pitch;
+  uint32_t* dst = slots + c * pitch;
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+}
+cudaError_t launch_lanes_scatter(const uint32_t* pitch_buf, int pitch, const uint32_t* lane_sizes,
+                                 const uint8_t* lane_first, uint32_t* slots, uint32_t* sizes, uint8_t* first, int iter,
+                                 int S, int B, cudaStream_t st) {
+  lanes_scatter_kernel<<<B, 256, 0, st>>>(pitch_buf, pitch, lane_sizes, lane_first, slots, sizes, first, iter, S);
+  return cudaGetLastError();
+}
+
+__global__ void lanes_gather_kernel(const unsigned long long* off, const uint32_t* sizes, const uint8_t* first,
+                                    long long n_bytes, int chunk_len, int c0, int S, int B,
+                                    unsigned long long* lane_off, uint32_t* lane_size, uint8_t* lane_first,
+                                    long long* lane_base, int* lane_len) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const long long c = (long long)c0 + (long long)b * S;
+  lane_off[b] = off[c];
+  lane_size[b] = sizes[c];
+  lane_first[b] = first[c];
+  lane_base[b] = c * chunk_len;
+  const long long rem = n_bytes - c * chunk_len;
+  lane_len[b] = (int)(rem < chunk_len ? (rem > 0 ? rem : 0) : chunk_len);
+}
+cudaError_t launch_lanes_gather(const unsigned long long* off, const uint32_t* sizes, const uint8_t* first,
+                                long long n_bytes, int chunk_len, int c0, int S, int B, unsigned long long* lane_off,
+                                uint32_t* lane_size, uint8_t* lane_first, long long* lane_base, int* lane_len,
+                                cudaStream_t st) {
+  lanes_gather_kernel<<<(B + 255) / 256, 256, 0, st>>>(off, sizes, first, n_bytes, chunk_len, c0, S, B, lane_off,
+                                                       lane_size, lane_first, lane_base, lane_len);
   return cudaGetLastError();
 }
 
 // decoder init (range_coder_kernels.cu:319-335) + raw first byte (:792-826)
 __global__ void dec_init_kernel(DecState* ds, const uint32_t* payload, const unsigned long long* off,
-                                const uint32_t* sizes, const uint8_t* first, uint8_t* out, long long n_bytes,
-                                int chunk_len, int B) {
+                                const uint32_t* sizes, const uint8_t* first, uint8_t* out, const long long* lane_base,
+                                const int* lane_len, int B) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   DecState s;
   dec_init(s, payload + off[b], (int)sizes[b]);
   ds[b] = s;
-  if (first && chunk_len_of(n_bytes, chunk_len, b) > 0) out[(long long)b * chunk_len] = first[b];
+  if (first && lane_len[b] > 0) out[lane_base[b]] = first[b];
 }
 cudaError_t launch_dec_init(DecState* ds, const uint32_t* payload, const unsigned long long* off, const uint32_t* sizes,
-                            const uint8_t* first, uint8_t* out, long long n_bytes, int chunk_len, int B,
+                            const uint8_t* first, uint8_t* out, const long long* lane_base, const int* lane_len, int B,
                             cudaStream_t st) {
-  dec_init_kernel<<<(B + 255) / 256, 256, 0, st>>>(ds, payload, off, sizes, first, out, n_bytes, chunk_len, B);
+  dec_init_kernel<<<(B + 255) / 256, 256, 0, st>>>(ds, payload, off, sizes, first, out, lane_base, lane_len, B);
   return cudaGetLastError();
 }
 cudaError_t launch_rc_decode_init(DecState* ds, const uint32_t* payload, const unsigned long long* off,
                                   const uint32_t* sizes, int n, cudaStream_t st) {
-  dec_init_kernel<<<(n + 255) / 256, 256, 0, st>>>(ds, payload, off, sizes, nullptr, nullptr, 0, 1, n);
+  dec_init_kernel<<<(n + 255) / 256, 256, 0, st>>>(ds, payload, off, sizes, nullptr, nullptr, nullptr, nullptr, n);
   return cudaGetLastError();
 }
 

@@ -99,6 +99,7 @@ struct boa_model {
   bool has_ext = false;
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;
   int cfg_batch = 0, cfg_tile = 0;
+  uint32_t warm = 0;  // interleave batch of warm-start lanes (0 = off)
 
   // weights (one arena)
   void* warena = nullptr;
@@ -120,6 +121,15 @@ struct boa_model {
   DecState* ds = nullptr;
   uint32_t* pitch_buf = nullptr;
   int* d_t = nullptr;
+  // per-lane views (decode) and per-lane results (interleaved compress)
+  unsigned long long* lane_off = nullptr;
+  uint32_t* lane_size = nullptr;
+  uint8_t* lane_first = nullptr;
+  long long* lane_base = nullptr;
+  int* lane_len = nullptr;
+  // per-chunk stream slots for interleaved compress (grow-only)
+  uint32_t* slots = nullptr;
+  size_t slots_words = 0;
   float* logits = nullptr;
   size_t logits_rows = 0;
 
@@ -151,6 +161,7 @@ boa_model::~boa_model() {
   for (auto e : ev_pool) cudaEventDestroy(e);
   if (warena) cudaFree(warena);
   if (work) cudaFree(work);
+  if (slots) cudaFree(slots);
   if (io) cudaFree(io);
   if (logits) cudaFree(logits);
   if (ev_in) cudaEventDestroy(ev_in);
@@ -247,6 +258,11 @@ int ensure_work(boa_model* m, size_t rows, size_t chunks, size_t pitch) {
       {(void**)&m->ds, al(chunks * sizeof(DecState))},
       {(void**)&m->pitch_buf, al(chunks * pitch * 4)},
       {(void**)&m->d_t, al(256)},
+      {(void**)&m->lane_off, al(chunks * 8)},
+      {(void**)&m->lane_size, al(chunks * 4)},
+      {(void**)&m->lane_first, al(chunks)},
+      {(void**)&m->lane_base, al(chunks * 8)},
+      {(void**)&m->lane_len, al(chunks * 4)},
   };
   if (m->backbone == BOA_BACKBONE_MAMBA) {
     plan.push_back({(void**)&m->conv_st, al((size_t)m->L * chunks * 3 * di * 4)});
@@ -389,6 +405,65 @@ void pick_batch(boa_model* m, uint32_t n_chunks, uint32_t chunk_len, bool compre
 }
 
 }  // namespace
+
+// Warm-start compress (boa.cpp:313-319, :395-435): W lanes, S = ceil(n/W)
+// iterations; in iteration `iter` lane b codes chunk iter + b*S with the model
+// state it carried from chunk iter - 1 + b*S (reset only at iter 0); every
+// chunk still gets its own range coder and raw first byte.
+int compress_interleaved(boa_model* m, const uint8_t* d_data, uint64_t n, uint32_t chunk_len, uint32_t n_chunks,
+                         uint8_t* d_first, uint32_t* d_payload, uint32_t* d_sizes, uint64_t* d_offsets) {
+  const int W = (int)std::min<uint32_t>(m->warm, n_chunks);
+  const int S = (int)((n_chunks + W - 1) / W);
+  const uint32_t pitch = boa_stream_capacity_words(chunk_len);
+  int T = m->cfg_tile > 0 ? m->cfg_tile : 64;
+  T = std::max(1, std::min<int>(T, (int)std::max<uint32_t>(1, chunk_len - 1)));
+  if (int rc = ensure_work(m, (size_t)W * T, W, pitch)) return rc;
+  const size_t need = (size_t)n_chunks * pitch;
+  if (need > m->slots_words) {
+    if (m->slots) { cudaStreamSynchronize(m->own); cudaFree(m->slots); m->slots = nullptr; m->slots_words = 0; }
+    if (cudaMalloc(&m->slots, need * 4) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(m, BOA_E_NOMEM, "device allocation of per-chunk stream slots failed");
+    }
+    m->slots_words = need;
+  }
+  cudaStream_t st = m->own;
+  uint32_t* lane_sizes = reinterpret_cast<uint32_t*>(m->lane_off);  // reuse per-lane scratch
+  if (int rc = reset_states(m, W)) return rc;
+  for (int iter = 0; iter < S; ++iter) {
+    int cur = 0;
+    while (cur < W && (uint64_t)cur * S + iter < n_chunks) ++cur;
+    if (cur == 0) break;
+    const uint8_t* data = d_data + (size_t)iter * chunk_len;
+    const long long rem = (long long)(n - (uint64_t)iter * chunk_len);
+    const long long stride = (long long)S * chunk_len;
+    BOA_LAUNCH(PC_OTHER, boa::launch_enc_init(m->es, cur, st));
+    BOA_LAUNCH(PC_OTHER, boa::launch_first_bytes(data, rem, chunk_len, stride, m->lane_first, cur, st));
+    // the carried state must have consumed exactly the chunk's bytes (all
+    // chunk_len positions, as forward_chunk does), so the last tile is
+    // shortened instead of padded
+    for (int t0 = 0; t0 < (int)chunk_len; t0 += T) {
+      const int Tt = std::min<int>(T, (int)chunk_len - t0);
+      boa::TokenSrc src{1, data, rem, (int)chunk_len, t0, Tt, nullptr, stride, nullptr, nullptr};
+      boa::GemmArgs h{};
+      h.tokens = data; h.n_bytes = rem; h.chunk_len = (int)chunk_len; h.stride = stride; h.t0 = t0; h.T = Tt;
+      h.lf = m->lf;
+      if (int rc = forward(m, src, cur, Tt, boa::EPI_HEAD_ENC, h)) return rc;
+      BOA_LAUNCH(PC_ENCODE, boa::launch_encode_tile(m->lf, m->es, m->pitch_buf, (int)pitch, cur, Tt, t0, rem,
+                                                    (int)chunk_len, stride, st));
+    }
+    BOA_LAUNCH(PC_OTHER, boa::launch_enc_finish(m->es, m->pitch_buf, (int)pitch, lane_sizes, cur, st));
+    BOA_LAUNCH(PC_OTHER, boa::launch_lanes_scatter(m->pitch_buf, (int)pitch, lane_sizes, m->lane_first, m->slots,
+                                                   d_sizes, d_first, iter, S, cur, st));
+  }
+  for (uint32_t c0 = 0; c0 < n_chunks; c0 += (uint32_t)W) {
+    const int Bb = (int)std::min<uint32_t>(W, n_chunks - c0);
+    BOA_LAUNCH(PC_OTHER, boa::launch_offsets(d_sizes + c0, (unsigned long long*)d_offsets + c0, Bb, st));
+    BOA_LAUNCH(PC_OTHER, boa::launch_compact(m->slots + (size_t)c0 * pitch, (int)pitch, d_sizes + c0,
+                                             (unsigned long long*)d_offsets + c0, d_payload, Bb, st));
+  }
+  return 0;
+}
 
 // =============================================================================
 extern "C" {
@@ -567,6 +642,12 @@ int boa_set_stream(boa_model* m, void* s) {
   return 0;
 }
 
+int boa_set_warm_start(boa_model* m, uint32_t interleave_batch) {
+  if (!m) return BOA_E_INVALID;
+  m->warm = interleave_batch;
+  return 0;
+}
+
 int boa_set_batch(boa_model* m, int chunks, int tile) {
   if (!m) return BOA_E_INVALID;
   if (chunks < 0 || tile < 0) return fail(m, BOA_E_INVALID, "batch and tile must be >= 0");
@@ -602,20 +683,22 @@ int boa_compress_device(boa_model* m, const uint8_t* d_data, uint64_t n, uint32_
   if (int rc = ensure_work(m, (size_t)B * T, B, pitch)) return rc;
   cudaStream_t st = m->own;
   BOA_CK(cudaMemsetAsync(d_offsets, 0, sizeof(uint64_t), st));
+  if (m->warm) return compress_interleaved(m, d_data, n, chunk_len, n_chunks, d_first, d_payload, d_sizes, d_offsets);
   for (uint32_t c0 = 0; c0 < n_chunks; c0 += B) {
     const int Bb = (int)std::min<uint32_t>(B, n_chunks - c0);
     const uint8_t* data = d_data + (size_t)c0 * chunk_len;
     const long long rem = (long long)(n - (uint64_t)c0 * chunk_len);
     if (int rc = reset_states(m, Bb)) return rc;
     BOA_LAUNCH(PC_OTHER, boa::launch_enc_init(m->es, Bb, st));
-    BOA_LAUNCH(PC_OTHER, boa::launch_first_bytes(data, rem, chunk_len, d_first + c0, Bb, st));
+    BOA_LAUNCH(PC_OTHER, boa::launch_first_bytes(data, rem, chunk_len, 0, d_first + c0, Bb, st));
     const int max_len = (int)std::min<long long>(chunk_len, rem);
     for (int t0 = 0; t0 < max_len - 1; t0 += T) {
       boa::TokenSrc src{1, data, rem, (int)chunk_len, t0, T, nullptr};
       boa::GemmArgs h{};
       h.tokens = data; h.n_bytes = rem; h.chunk_len = (int)chunk_len; h.t0 = t0; h.T = T; h.lf = m->lf;
       if (int rc = forward(m, src, Bb, T, boa::EPI_HEAD_ENC, h)) return rc;
-      BOA_LAUNCH(PC_ENCODE, boa::launch_encode_tile(m->lf, m->es, m->pitch_buf, (int)pitch, Bb, T, t0, rem, (int)chunk_len, st));
+      BOA_LAUNCH(PC_ENCODE, boa::launch_encode_tile(m->lf, m->es, m->pitch_buf, (int)pitch, Bb, T, t0, rem,
+                                                    (int)chunk_len, 0, st));
     }
     BOA_LAUNCH(PC_OTHER, boa::launch_enc_finish(m->es, m->pitch_buf, (int)pitch, d_sizes + c0, Bb, st));
     BOA_LAUNCH(PC_OTHER, boa::launch_offsets(d_sizes + c0, (unsigned long long*)d_offsets + c0, Bb, st));
@@ -631,57 +714,89 @@ int boa_decompress_device(boa_model* m, const uint32_t* d_payload, const uint64_
   if (chunk_len == 0 || n_chunks == 0 || (uint64_t)(n_chunks - 1) * chunk_len >= n)
     return fail(m, BOA_E_INVALID, "chunk geometry does not match n_bytes");
   StreamScope scope(m);
+  // lanes: warm start -> W lanes over S interleaved iterations (lane b holds
+  // chunk iter + b*S, state carried); otherwise batches of consecutive chunks
   int B, T;
-  pick_batch(m, n_chunks, chunk_len, false, B, T);
+  int S = 1, iters;
+  if (m->warm) {
+    B = (int)std::min<uint32_t>(m->warm, n_chunks);
+    S = (int)((n_chunks + B - 1) / B);
+    iters = S;
+  } else {
+    pick_batch(m, n_chunks, chunk_len, false, B, T);
+    iters = (int)((n_chunks + B - 1) / B);
+  }
   if (int rc = ensure_work(m, (size_t)B, B, 1)) return rc;
   cudaStream_t st = m->own;
-  for (uint32_t c0 = 0; c0 < n_chunks; c0 += B) {
-    const int Bb = (int)std::min<uint32_t>(B, n_chunks - c0);
-    const long long rem = (long long)(n - (uint64_t)c0 * chunk_len);
-    uint8_t* out = d_out + (size_t)c0 * chunk_len;
-    if (int rc = reset_states(m, Bb)) return rc;
-    BOA_LAUNCH(PC_OTHER, boa::launch_dec_init(m->ds, d_payload, (const unsigned long long*)d_offsets + c0, d_sizes + c0,
-                                d_first + c0, out, rem, chunk_len, Bb, st));
+  cudaGraphExec_t exec = nullptr;
+  int exec_lanes = -1;
+  uint64_t per_step = 0;
+  auto done = [&](int rc) {
+    if (exec) cudaGraphExecDestroy(exec);
+    return rc;
+  };
+  for (int it = 0; it < iters; ++it) {
+    const int c0 = m->warm ? it : it * B;
+    int cur;
+    if (m->warm) {
+      cur = 0;
+      while (cur < B && (uint64_t)cur * S + c0 < n_chunks) ++cur;
+    } else {
+      cur = (int)std::min<uint32_t>(B, n_chunks - (uint32_t)c0);
+    }
+    if (cur <= 0) break;
+    if (!m->warm || it == 0)
+      if (int rc = reset_states(m, cur)) return done(rc);
+    BOA_LAUNCH(PC_OTHER, boa::launch_lanes_gather((const unsigned long long*)d_offsets, d_sizes, d_first, (long long)n,
+                                                  (int)chunk_len, c0, S, cur, m->lane_off, m->lane_size,
+                                                  m->lane_first, m->lane_base, m->lane_len, st));
+    BOA_LAUNCH(PC_OTHER, boa::launch_dec_init(m->ds, d_payload, m->lane_off, m->lane_size, m->lane_first, d_out,
+                                              m->lane_base, m->lane_len, cur, st));
     BOA_LAUNCH(PC_OTHER, boa::launch_set_counter(m->d_t, 1, st));
-    const int max_len = (int)std::min<long long>(chunk_len, rem);
-    if (max_len <= 1) continue;
-    boa::TokenSrc src{2, out, rem, (int)chunk_len, 0, 1, m->d_t};
+    const int max_len = (int)std::min<long long>(chunk_len, (long long)n - (long long)c0 * chunk_len);
+    if (max_len <= 1 && !m->warm) continue;
+    boa::TokenSrc src{2, d_out, (long long)n, (int)chunk_len, 0, 1, m->d_t, 0, m->lane_base, m->lane_len};
     boa::GemmArgs h{};
-    h.out_bytes = out; h.n_bytes = rem; h.chunk_len = (int)chunk_len; h.d_t = m->d_t; h.dstates = m->ds;
-    h.payload = d_payload; h.offsets = (const unsigned long long*)d_offsets + c0;
+    h.out_bytes = d_out; h.n_bytes = (long long)n; h.chunk_len = (int)chunk_len; h.d_t = m->d_t; h.dstates = m->ds;
+    h.payload = d_payload; h.offsets = m->lane_off; h.lane_base = m->lane_base; h.lane_len = m->lane_len;
     if (m->prof) {  // eager steps so every launch is bracketed by events
-      for (int t = 1; t < max_len; ++t) {
-        if (int rc = forward(m, src, Bb, 1, boa::EPI_HEAD_DEC, h)) return rc;
+      for (int t = 1; t <= (m->warm ? max_len : max_len - 1); ++t) {
+        if (int rc = forward(m, src, cur, 1, boa::EPI_HEAD_DEC, h)) return done(rc);
         BOA_LAUNCH(PC_OTHER, boa::launch_increment(m->d_t, st));
       }
       continue;
     }
-    // capture one step (model + fused decode + counter) and replay it
-    // max_len - 1 times (boa.cpp:736-756)
-    cudaGraph_t graph = nullptr;
-    cudaGraphExec_t exec = nullptr;
-    const uint64_t l0 = m->launches;
-    BOA_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    int rc = forward(m, src, Bb, 1, boa::EPI_HEAD_DEC, h);
-    cudaError_t ei = boa::launch_increment(m->d_t, st);
-    cudaError_t ee = cudaStreamEndCapture(st, &graph);
-    const uint64_t per_step = m->launches - l0 + 1;
-    m->launches = l0;
-    if (rc) { if (graph) cudaGraphDestroy(graph); return rc; }
-    if (ei != cudaSuccess) { if (graph) cudaGraphDestroy(graph); return cuda_fail(m, ei, "capture increment"); }
-    if (ee != cudaSuccess) return cuda_fail(m, ee, "cudaStreamEndCapture");
-    cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
-    cudaGraphDestroy(graph);
-    if (e != cudaSuccess) return cuda_fail(m, e, "cudaGraphInstantiate");
-    for (int t = 1; t < max_len; ++t) {
-      e = cudaGraphLaunch(exec, st);
-      if (e != cudaSuccess) break;
+    if (exec_lanes != cur) {
+      // capture one step (model + fused decode + counter); every per-lane
+      // quantity is read from device arrays, so the graph serves every
+      // iteration with this many lanes (boa.cpp:736-756)
+      if (exec) { cudaGraphExecDestroy(exec); exec = nullptr; }
+      cudaGraph_t graph = nullptr;
+      const uint64_t l0 = m->launches;
+      BOA_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+      int rc = forward(m, src, cur, 1, boa::EPI_HEAD_DEC, h);
+      cudaError_t ei = boa::launch_increment(m->d_t, st);
+      cudaError_t ee = cudaStreamEndCapture(st, &graph);
+      per_step = m->launches - l0 + 1;
+      m->launches = l0;
+      if (rc) { if (graph) cudaGraphDestroy(graph); return done(rc); }
+      if (ei != cudaSuccess) { if (graph) cudaGraphDestroy(graph); return done(cuda_fail(m, ei, "capture increment")); }
+      if (ee != cudaSuccess) return done(cuda_fail(m, ee, "cudaStreamEndCapture"));
+      cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+      cudaGraphDestroy(graph);
+      if (e != cudaSuccess) { exec = nullptr; return done(cuda_fail(m, e, "cudaGraphInstantiate")); }
+      exec_lanes = cur;
+    }
+    // warm start: one more step feeds the chunk's last byte into the carried
+    // state (the encoder's forward pass consumed it); no byte is decoded then
+    const int steps = m->warm ? max_len : max_len - 1;
+    for (int t = 1; t <= steps; ++t) {
+      cudaError_t e = cudaGraphLaunch(exec, st);
+      if (e != cudaSuccess) return done(cuda_fail(m, e, "cudaGraphLaunch"));
       m->launches += per_step;
     }
-    cudaGraphExecDestroy(exec);
-    if (e != cudaSuccess) return cuda_fail(m, e, "cudaGraphLaunch");
   }
-  return 0;
+  return done(0);
 }
 
 int boa_compress_chunks(boa_model* m, const uint8_t* data, size_t n, uint32_t chunk_len, uint32_t first_chunk,

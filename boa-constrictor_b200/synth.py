@@ -149,3 +149,25 @@ def exact_logit_weights(d_model: int, n_layers: int, seed: int, support, low: fl
             a[np.asarray(list(support), dtype=np.int64)] = 0.0
         out.append((name, a))
     return out
+
+
+def markov_stream(n_bytes: int, seed: int, alpha: float = 0.05) -> bytes:
+    """Order-2 Markov byte source: each of the 65536 contexts
+    (previous two bytes) has its own next-byte distribution drawn from
+    Dirichlet(alpha * 1_256) with ``numpy.random.default_rng(seed)``; the
+    stream starts from context (0, 0) and draws each byte by inverse CDF from
+    uniforms of the same generator (drawn after the tables)."""
+    rng = np.random.default_rng(seed)
+    g = rng.gamma(alpha, 1.0, size=(65536, 256))
+    g /= g.sum(axis=1, keepdims=True)
+    cdf = np.cumsum(g, axis=1)
+    u = rng.random(n_bytes)
+    out = np.empty(n_bytes, np.uint8)
+    a = b = 0
+    for i in range(n_bytes):
+        row = cdf[(a << 8) | b]
+        s = int(np.searchsorted(row, u[i] * row[-1], side="right"))
+        s = 255 if s > 255 else s
+        out[i] = s
+        a, b = b, s
+    return out.tobytes()

@@ -64,6 +64,12 @@ int boa_set_stream(boa_model* h, void* cuda_stream);
  * (--tile, boa.cpp:313-316).  0 = automatic from free device memory
  * (auto_size_params, boa.cpp:109-156). */
 int boa_set_batch(boa_model* h, int chunks_per_batch, int tile_tokens);
+/* --warm-start (boa.cpp:313-319, :395-435, :608-610): with interleave_batch
+ * W > 0 the codec runs W lanes; lane b codes chunks b*S, b*S+1, ... with
+ * S = ceil(n_chunks / W), carrying the model state from chunk to chunk (each
+ * chunk still has its own range coder and raw first byte).  A container made
+ * this way records flags bit0 and W; decode it with the same W.  0 = off. */
+int boa_set_warm_start(boa_model* h, uint32_t interleave_batch);
 /* Per-chunk stream capacity in 32-bit words used on the device for a chunk
  * length (a tight bound: <= 24.01 bits per byte plus the flush words). */
 uint32_t boa_stream_capacity_words(uint32_t chunk_len);

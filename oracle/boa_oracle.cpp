@@ -637,4 +637,77 @@ int orc_decompress(void* mp, const uint32_t* stream_words, uint32_t pitch, const
   return 0;
 }
 
+// Warm start (boa.cpp:313-319, :395-435): W lanes; lane b codes chunks
+// b*S .. b*S+S-1 (S = ceil(n_chunks / W)) in order, carrying the model state;
+// the encoder's forward pass consumes every byte of a chunk (forward_chunk
+// over all chunk_size positions), each chunk has its own coder and raw first
+// byte.  The decoder feeds a chunk's last byte into the state before moving
+// to the lane's next chunk, so it follows the encoder.
+int orc_compress_warm(void* mp, const uint8_t* data, size_t n, uint32_t chunk_len, uint32_t W, float inv_t,
+                      int n_threads, uint8_t* first_bytes, uint32_t* stream_words, uint32_t pitch, uint32_t* sizes) {
+  const Model& M = *(Model*)mp;
+  if (chunk_len == 0 || W == 0) { g_err = "chunk_len and W must be > 0"; return -1; }
+  const int n_chunks = (int)((n + chunk_len - 1) / chunk_len);
+  const int Wl = std::min<int>((int)W, n_chunks), S = (n_chunks + Wl - 1) / Wl;
+  std::atomic<int> bad(0);
+  parallel_for(Wl, n_threads, [&](int b) {
+    State st; st.init(M); Scratch s;
+    std::vector<float> lg((size_t)chunk_len * 256);
+    uint32_t Q[257];
+    for (int i = 0; i < S; ++i) {
+      const int c = b * S + i;
+      if (c >= n_chunks) break;
+      const size_t off = (size_t)c * chunk_len;
+      const int len = (int)std::min<size_t>(chunk_len, n - off);
+      const uint8_t* tk = data + off;
+      first_bytes[c] = tk[0];
+      Enc enc;
+      uint32_t* out = stream_words + (size_t)c * pitch;
+      predictor_forward(M, st, tk, len, lg.data(), s);
+      for (int t = 0; t + 1 < len; ++t) {
+        cdf_row(lg.data() + (size_t)t * 256, inv_t, Q);
+        const int sym = tk[t + 1];
+        if (!enc_symbol(enc, Q[sym], Q[sym + 1] - Q[sym], out, (int)pitch)) { bad = 1; return; }
+      }
+      const int w = enc_finish(enc, out, (int)pitch);
+      if (w < 0) { bad = 1; return; }
+      sizes[c] = (uint32_t)w;
+    }
+  });
+  if (bad) { g_err = "stream exceeded pitch"; return -1; }
+  return 0;
+}
+
+int orc_decompress_warm(void* mp, const uint32_t* stream_words, uint32_t pitch, const uint32_t* sizes,
+                        const uint8_t* first_bytes, size_t n, uint32_t chunk_len, uint32_t W, float inv_t,
+                        int n_threads, uint8_t* out) {
+  const Model& M = *(Model*)mp;
+  if (chunk_len == 0 || W == 0) { g_err = "chunk_len and W must be > 0"; return -1; }
+  const int n_chunks = (int)((n + chunk_len - 1) / chunk_len);
+  const int Wl = std::min<int>((int)W, n_chunks), S = (n_chunks + Wl - 1) / Wl;
+  parallel_for(Wl, n_threads, [&](int b) {
+    State st; st.init(M); Scratch s;
+    float lg[256]; uint32_t Q[257];
+    for (int i = 0; i < S; ++i) {
+      const int c = b * S + i;
+      if (c >= n_chunks) break;
+      const size_t off = (size_t)c * chunk_len;
+      const int len = (int)std::min<size_t>(chunk_len, n - off);
+      uint8_t* o = out + off;
+      o[0] = first_bytes[c];
+      Dec dec; dec.init(stream_words + (size_t)c * pitch, (int)sizes[c]);
+      for (int t = 1; t < len; ++t) {
+        predictor_forward(M, st, o + t - 1, 1, lg, s);
+        cdf_row(lg, inv_t, Q);
+        uint32_t lo, hi;
+        const int sym = dec_search(Q, dec.target(), lo, hi);
+        o[t] = (uint8_t)sym;
+        dec.update(lo, hi);
+      }
+      predictor_forward(M, st, o + len - 1, 1, lg, s);  // the chunk's last byte
+    }
+  });
+  return 0;
+}
+
 }  // extern "C"

@@ -61,6 +61,14 @@ int orc_decompress(void* model, const uint32_t* stream_words, uint32_t pitch_wor
                    size_t n, uint32_t chunk_len, float inv_temperature, int n_threads,
                    uint8_t* out);
 
+/* Warm start: W lanes, lane b codes chunks b*S .. b*S+S-1 with carried state. */
+int orc_compress_warm(void* model, const uint8_t* data, size_t n, uint32_t chunk_len, uint32_t W,
+                      float inv_temperature, int n_threads, uint8_t* first_bytes, uint32_t* stream_words,
+                      uint32_t pitch_words, uint32_t* sizes_words);
+int orc_decompress_warm(void* model, const uint32_t* stream_words, uint32_t pitch_words,
+                        const uint32_t* sizes_words, const uint8_t* first_bytes, size_t n, uint32_t chunk_len,
+                        uint32_t W, float inv_temperature, int n_threads, uint8_t* out);
+
 #ifdef __cplusplus
 }
 #endif

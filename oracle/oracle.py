@@ -45,6 +45,10 @@ def lib():
                                    _u8p, _u32p, C.c_uint32, _u32p]
         L.orc_decompress.argtypes = [C.c_void_p, _u32p, C.c_uint32, _u32p, _u8p, C.c_size_t,
                                      C.c_uint32, C.c_float, C.c_int, _u8p]
+        L.orc_compress_warm.argtypes = [C.c_void_p, _u8p, C.c_size_t, C.c_uint32, C.c_uint32, C.c_float, C.c_int,
+                                        _u8p, _u32p, C.c_uint32, _u32p]
+        L.orc_decompress_warm.argtypes = [C.c_void_p, _u32p, C.c_uint32, _u32p, _u8p, C.c_size_t, C.c_uint32,
+                                          C.c_uint32, C.c_float, C.c_int, _u8p]
         _lib = L
     return _lib
 
@@ -78,7 +82,8 @@ class OracleModel:
         lib().orc_logits(self.h, _p(tokens, _u8p), B, L, mode, _p(out, _f32p))
         return out
 
-    def compress(self, data: bytes, chunk_len: int, inv_temperature: float = 1.0, threads: int = 0):
+    def compress(self, data: bytes, chunk_len: int, inv_temperature: float = 1.0, threads: int = 0,
+                 warm: int = 0):
         n = len(data)
         nc = (n + chunk_len - 1) // chunk_len
         pw = pitch_words(chunk_len)
@@ -86,16 +91,21 @@ class OracleModel:
         fb = np.zeros(max(nc, 1), np.uint8)
         words = np.zeros(max(nc, 1) * pw, np.uint32)
         sizes = np.zeros(max(nc, 1), np.uint32)
-        rc = lib().orc_compress(self.h, _p(arr, _u8p), n, chunk_len, inv_temperature,
-                                threads or os.cpu_count(), _p(fb, _u8p), _p(words, _u32p), pw,
-                                _p(sizes, _u32p))
+        if warm:
+            rc = lib().orc_compress_warm(self.h, _p(arr, _u8p), n, chunk_len, warm, inv_temperature,
+                                         threads or os.cpu_count(), _p(fb, _u8p), _p(words, _u32p), pw,
+                                         _p(sizes, _u32p))
+        else:
+            rc = lib().orc_compress(self.h, _p(arr, _u8p), n, chunk_len, inv_temperature,
+                                    threads or os.cpu_count(), _p(fb, _u8p), _p(words, _u32p), pw,
+                                    _p(sizes, _u32p))
         if rc != 0:
             raise RuntimeError(lib().orc_last_error().decode())
         streams = [words[i * pw: i * pw + sizes[i]].copy() for i in range(nc)]
         return fb[:nc].copy(), streams
 
     def decompress(self, first_bytes, streams, n: int, chunk_len: int,
-                   inv_temperature: float = 1.0, threads: int = 0) -> bytes:
+                   inv_temperature: float = 1.0, threads: int = 0, warm: int = 0) -> bytes:
         nc = len(streams)
         pw = pitch_words(chunk_len)
         words = np.zeros(max(nc, 1) * pw, np.uint32)
@@ -107,8 +117,12 @@ class OracleModel:
         if fb.size == 0:
             fb = np.zeros(1, np.uint8)
         out = np.zeros(max(n, 1), np.uint8)
-        lib().orc_decompress(self.h, _p(words, _u32p), pw, _p(sizes, _u32p), _p(fb, _u8p), n,
-                             chunk_len, inv_temperature, threads or os.cpu_count(), _p(out, _u8p))
+        if warm:
+            lib().orc_decompress_warm(self.h, _p(words, _u32p), pw, _p(sizes, _u32p), _p(fb, _u8p), n,
+                                      chunk_len, warm, inv_temperature, threads or os.cpu_count(), _p(out, _u8p))
+        else:
+            lib().orc_decompress(self.h, _p(words, _u32p), pw, _p(sizes, _u32p), _p(fb, _u8p), n,
+                                 chunk_len, inv_temperature, threads or os.cpu_count(), _p(out, _u8p))
         return out[:n].tobytes()
 
 

@@ -215,3 +215,88 @@ def test_d512_logits_forms_and_roundtrip(boa, oracle, weights):
     assert np.array_equal(lg, m.logits(tok, 1))
     data = boa.synth.particle_stream(3 * 700 + 5, 4)
     _roundtrip(boa, m, data, 700)
+
+
+def test_fp16_weight_file(boa, oracle, wdir):
+    """"BOA\\1" files (fp16 tensors, convert_boa_weights.py:174-177) load on
+    both sides; logits agree with the oracle reading the same file."""
+    p = str(wdir / "w_fp16.bin")
+    boa.synth.write_random_weights(p, "mamba", 256, 2, 8, fp16=True)
+    m = boa.Model(p, "mamba", 256, 2)
+    tok = np.random.default_rng(15).integers(0, 256, (2, 33), dtype=np.uint8)
+    ref = oracle.OracleModel(p, 0, 256, 2).logits(tok, 0)
+    lg = m.logits(tok, 0)
+    assert np.abs(lg - ref).max() <= LOGIT_RTOL * np.abs(ref).max()
+
+
+def test_configs3_mingru_d256_L8_markov(boa, oracle, weights):
+    """configs[3] geometry: minGRU d256 / 8 layers (seed 2) on the order-2
+    Markov source; logits vs the oracle, both forms bitwise, byte-exact round
+    trip."""
+    p = weights("mingru", 256, 8, 2)
+    m = boa.Model(p, "mingru", 256, 8)
+    data = boa.synth.markov_stream(6000, 3)
+    tok = np.frombuffer(data[:2 * 48], np.uint8).reshape(2, 48)
+    ref = oracle.OracleModel(p, 3, 256, 8).logits(tok, 0)
+    lg = m.logits(tok, 0)
+    assert np.abs(lg - ref).max() <= LOGIT_RTOL * np.abs(ref).max()
+    assert np.array_equal(lg, m.logits(tok, 1))
+    _roundtrip(boa, m, data, 2000)
+
+
+@pytest.mark.parametrize("n,chunk,W,tile", [(11 * 300 + 17, 300, 4, 0), (8 * 256, 256, 3, 50), (5 * 700 + 1, 700, 2, 0)])
+def test_warm_start_roundtrip(boa, m64, n, chunk, W, tile):
+    """--warm-start: W lanes carry the model state across their chunks; the
+    last chunk may be one byte (zero-word stream)."""
+    data = boa.synth.particle_stream(n, 21)
+    m64.set_warm_start(W)
+    m64.set_batch(0, tile)
+    try:
+        _roundtrip(boa, m64, data, chunk)
+    finally:
+        m64.set_warm_start(0)
+        m64.set_batch(0, 0)
+
+
+def test_warm_start_with_one_chunk_per_lane_equals_plain(boa, m64):
+    """W >= n_chunks gives every lane a single chunk (fresh state), so the
+    streams must equal the plain path's bit for bit."""
+    data = boa.synth.particle_stream(6 * 400 + 9, 22)
+    plain = m64.compress(data, 400)
+    m64.set_warm_start(7)
+    try:
+        warm = m64.compress(data, 400)
+    finally:
+        m64.set_warm_start(0)
+    assert all(np.array_equal(a, b) for a, b in zip(plain, warm))
+
+
+def test_warm_start_state_carry_matters(boa, m256):
+    """With carried state the streams differ from the plain path (the lanes
+    really carry state) yet still round-trip."""
+    data = boa.synth.particle_stream(8 * 512, 23)
+    plain = m256.compress(data, 512)
+    m256.set_warm_start(2)
+    try:
+        warm = m256.compress(data, 512)
+        back = m256.decompress(warm[0], warm[1], warm[2], [512] * 8, 512)
+    finally:
+        m256.set_warm_start(0)
+    assert back == data
+    assert np.array_equal(plain[1][[0, 4]], warm[1][[0, 4]])  # lane heads start fresh
+    assert not np.array_equal(plain[2], warm[2])
+
+
+def test_cli_warm_start_roundtrip(boa, weights, tmp_path):
+    data = boa.synth.particle_stream(9000, 24)
+    src, enc, dec = tmp_path / "in.bin", tmp_path / "x.boa", tmp_path / "out.bin"
+    src.write_bytes(data)
+    w = weights("mamba", 64, 2, 3)
+    r = subprocess.run([boa.CLI_PATH, "compress", w, str(src), str(enc), "64", "2", "--chunk-size", "1000",
+                        "--gpu-batch", "3", "--warm-start"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    p = boa.boa2_parse(enc.read_bytes())
+    assert p["flags"] == 1 and p["interleave_batch"] == 3
+    r = subprocess.run([boa.CLI_PATH, "decompress", w, str(enc), str(dec), "64", "2"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    assert dec.read_bytes() == data

@@ -94,3 +94,13 @@ def test_oracle_mingru_roundtrip(oracle, weights):
     a = m.logits(np.frombuffer(data[:64], np.uint8).reshape(2, 32), 0)
     b = m.logits(np.frombuffer(data[:64], np.uint8).reshape(2, 32), 1)
     assert np.array_equal(a, b)
+
+
+def test_oracle_warm_start_roundtrip(oracle, boa, weights):
+    m = oracle.OracleModel(weights("mamba", 64, 2, 3), 0, 64, 2)
+    data = boa.synth.particle_stream(11 * 300 + 17, 7)
+    fb, st = m.compress(data, 300, warm=4)
+    assert m.decompress(fb, st, len(data), 300, warm=4) == data
+    fb1, st1 = m.compress(data, 300, warm=12)  # one chunk per lane == plain
+    fb0, st0 = m.compress(data, 300)
+    assert all(np.array_equal(a, b) for a, b in zip(st0, st1))
