@@ -12,6 +12,8 @@ manifest.json, so only reference OUTPUTS are stored):
   ref_exact.boa          reference CLI compress of a seeded byte stream under
                          an exact-logit model (synth.exact_logit_weights):
                          pins quantiser + range coder + BOA2 container bit-exact
+  ref_exact_warm.boa     the same with --warm-start --gpu-batch 3: pins the
+                         warm-start container fields (flags bit0, batch)
   ref_rand_d256L8.boa    reference CLI compress of 64 KiB of particle records
                          under the configs[0] model: container layout and the
                          reference's bits/byte
@@ -99,6 +101,14 @@ def main(out_dir):
                                boa_sha=sha(open(boa, "rb").read()),
                                ref_roundtrip=open(back, "rb").read() == data)
 
+    boa_w = os.path.join(out_dir, "ref_exact_warm.boa")
+    run([os.path.join(REF, "boa_constrictor"), "compress", w, fin, boa_w, str(EXACT["d_model"]),
+         str(EXACT["n_layers"]), "--gpu-batch", "3", "--chunk-size", str(EXACT["chunk"]), "--warm-start"])
+    back_w = os.path.join(tmp, "exact_warm.out")
+    run([os.path.join(REF, "boa_constrictor"), "decompress", w, boa_w, back_w, str(EXACT["d_model"]),
+         str(EXACT["n_layers"])])
+    man["exact_warm_result"] = dict(boa_bytes=os.path.getsize(boa_w), ref_roundtrip=open(back_w, "rb").read() == data)
+
     # random-init configs[0] model on particle records
     w = os.path.join(tmp, "w_rand.bin")
     synth.write_random_weights(w, "mamba", RAND["d_model"], RAND["n_layers"], RAND["seed"])
@@ -114,6 +124,14 @@ def main(out_dir):
                               boa_sha=sha(open(boa, "rb").read()),
                               bits_per_byte=8.0 * os.path.getsize(boa) / len(data),
                               ref_roundtrip=open(back, "rb").read() == data)
+    # the reference's own warm-start round trip on the same model and data
+    boa_rw = os.path.join(tmp, "rand_warm.boa")
+    run([os.path.join(REF, "boa_constrictor"), "compress", w, fin, boa_rw, str(RAND["d_model"]),
+         str(RAND["n_layers"]), "--gpu-batch", "4", "--chunk-size", str(RAND["chunk"]), "--warm-start"])
+    back_rw = os.path.join(tmp, "rand_warm.out")
+    run([os.path.join(REF, "boa_constrictor"), "decompress", w, boa_rw, back_rw, str(RAND["d_model"]),
+         str(RAND["n_layers"])])
+    man["rand_warm_result"] = dict(ref_roundtrip=open(back_rw, "rb").read() == data)
     for f in os.listdir(tmp):
         os.remove(os.path.join(tmp, f))
     os.rmdir(tmp)

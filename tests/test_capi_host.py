@@ -142,3 +142,13 @@ def test_container_rejects_damaged_files(boa, damage):
     with pytest.raises(boa.BoaError) as e:
         boa.boa2_parse(bytes(blob))
     assert e.value.code == boa.BOA_E_FORMAT
+
+
+def test_reference_warm_start_container_fields(boa, boa2, manifest):
+    blob = open(os.path.join(GOLDEN, "ref_exact_warm.boa"), "rb").read()
+    p = boa.boa2_parse(blob)
+    assert p["flags"] == 1 and p["interleave_batch"] == 3
+    assert p["streams"] == boa2.parse(blob)["streams"]
+    # the reference's own warm-start round trip fails on a real model
+    # (recorded by make_golden.py); ours is tested in test_gpu_parity.py
+    assert manifest["rand_warm_result"]["ref_roundtrip"] is False

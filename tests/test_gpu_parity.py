@@ -300,3 +300,20 @@ def test_cli_warm_start_roundtrip(boa, weights, tmp_path):
     r = subprocess.run([boa.CLI_PATH, "decompress", w, str(enc), str(dec), "64", "2"], capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
     assert dec.read_bytes() == data
+
+
+def test_warm_start_container_matches_reference_binary(boa, manifest, golden_mod, wdir):
+    """The reference CLI with --warm-start --gpu-batch 3 on the exact-logit
+    model (whose logits do not depend on the carried state) wrote
+    ref_exact_warm.boa; ours must be byte-identical, flags and batch included."""
+    E = manifest["exact"]
+    p = str(wdir / "exact_gpu_w.bin")
+    boa.synth.write_weights(p, boa.synth.exact_logit_weights(E["d_model"], E["n_layers"], E["seed"], E["support"]))
+    m = boa.Model(p, "mamba", E["d_model"], E["n_layers"])
+    data = golden_mod.exact_input(E)
+    m.set_warm_start(3)
+    fb, sizes, pay = m.compress(data, E["chunk"])
+    blob = boa.boa2_build(len(data), E["chunk"], fb, sizes, pay, warm_start=3)
+    assert blob == open(f"{GOLDEN}/ref_exact_warm.boa", "rb").read()
+    lens = [E["chunk"]] * (len(sizes) - 1) + [len(data) - (len(sizes) - 1) * E["chunk"]]
+    assert m.decompress(fb, sizes, pay, lens, E["chunk"]) == data
