@@ -29,7 +29,7 @@ CLI_PATH = os.path.join(HERE, "bin", "boa_constrictor")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "boa_b200.h")
 
 BOA_OK, BOA_E_INVALID, BOA_E_CUDA, BOA_E_IO, BOA_E_FORMAT, BOA_E_DEVICE, BOA_E_NOMEM = 0, -1, -2, -3, -4, -5, -6
-BACKBONES = {"mamba": 0, "mambav1": 0, "mingru": 3}
+BACKBONES = {"mamba": 0, "mambav1": 0, "lstm": 1, "gru": 2, "mingru": 3}
 PROF_CLASSES = 12
 
 _u8p, _u32p, _u64p, _f32p = (C.POINTER(C.c_uint8), C.POINTER(C.c_uint32), C.POINTER(C.c_uint64),

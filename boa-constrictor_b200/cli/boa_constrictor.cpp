@@ -2,7 +2,7 @@
 // (portability_solved_cpp/boa.cpp:819-942):
 //
 //   boa_constrictor <compress|decompress> <model.bin> <input> <output>
-//                   [d_model] [n_layers] [--backbone mamba|mingru]
+//                   [d_model] [n_layers] [--backbone mamba|lstm|gru|mingru]
 //                   [--gpu-batch B] [--max-chunks C] [--chunk-size S] [--tile T]
 //                   [--temperature T] [--show-timings] [--no-graph] [--gpus N]
 //
@@ -43,6 +43,8 @@ bool read_file(const std::string& p, std::vector<uint8_t>& v) {
 
 int backbone_code(const std::string& s) {
   if (s == "mamba" || s == "mambav1") return BOA_BACKBONE_MAMBA;
+  if (s == "lstm") return BOA_BACKBONE_LSTM;
+  if (s == "gru") return BOA_BACKBONE_GRU;
   if (s == "mingru") return BOA_BACKBONE_MINGRU;
   return -1;
 }
@@ -194,7 +196,7 @@ int do_decompress(const Opts& o) {
 int main(int argc, char** argv) {
   if (argc < 5) {
     std::cerr << "Usage: boa_constrictor <compress|decompress> <model> <input> <output> [d_model] [n_layers] "
-                 "[--backbone mamba|mingru] [--gpu-batch B] [--max-chunks C] [--chunk-size S] [--tile T] "
+                 "[--backbone mamba|lstm|gru|mingru] [--gpu-batch B] [--max-chunks C] [--chunk-size S] [--tile T] "
                  "[--temperature T] [--show-timings] [--no-graph] [--gpus N]\n";
     return 1;
   }

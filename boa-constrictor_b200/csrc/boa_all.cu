@@ -4,6 +4,7 @@
 // device code.
 #include "gemm.cu"
 #include "mamba.cu"
+#include "rnn.cu"
 #include "runtime.cpp"
 #include "container.cpp"
 #include "noalloc.cu"

@@ -742,6 +742,8 @@ static int pick_bn(int mode, int N) {
   if ((mode == EPI_LN_SPLIT || mode == EPI_RES_LN) && N == 512) return 512;
   if (mode == EPI_LN_SPLIT || mode == EPI_RES_LN || mode >= EPI_LOGITS) return N;
   if (N % 256 == 0) return 256;
+  if (N % 128 == 0 && N > 128) return 128;  // 384 (GRU gates at d=128)
+  if (N % 64 == 0 && N > 128) return 64;    // 192 (GRU gates at d=64)
   return N;
 }
 

@@ -45,6 +45,14 @@ cudaError_t scan_prepare_device();
 // into x_out rows (boa_gpu.hpp:652-693).  zh = [M][2d] (z logits | h~ raw).
 cudaError_t launch_mingru(const float* zh, int d, float* h_state, float* x_out, int B, int T, cudaStream_t st);
 
+// LSTM / GRU gate update for position t of a T-position tile: reads
+// ih [B*T][G] row b*T+t and hh [B][G] (G = 4d LSTM, 3d GRU), updates h_state
+// (and c_state for LSTM) [B][d], writes h to x_out row b*T+t and its bf16
+// hi/lo split to hl [2][B][d] (plane elements apart).
+cudaError_t launch_rnn_gates(bool lstm, const float* ih, const float* hh, int d, int t, int T, float* h_state,
+                             float* c_state, __nv_bfloat16* hl, long long hl_plane, float* x_out, int B,
+                             cudaStream_t st);
+
 // x += y (residual), then xn = split(LN(x)) -- minGRU blocks
 cudaError_t launch_add_ln(float* x, const float* y, int d, __nv_bfloat16* xn, long long plane,
                           const float* ln_w, const float* ln_b, int M, cudaStream_t st);

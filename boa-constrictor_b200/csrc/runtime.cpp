@@ -43,6 +43,9 @@ struct LayerW {
   // minGRU: [Wz; Wh] stacked into one N = 2d projection
   HL zh;
   float* zh_b;
+  // LSTM / GRU: input and recurrent projections, N = G = 4d / 3d
+  HL ih, hh;
+  float *ih_b, *hh_b;
 };
 
 uint16_t f2bf(float f) {  // round to nearest even
@@ -116,6 +119,8 @@ struct boa_model {
   float *x = nullptr, *xz = nullptr, *u = nullptr, *delta = nullptr;
   bf16 *xn = nullptr, *uhl = nullptr;
   float *conv_st = nullptr, *ssm_st = nullptr, *h_st = nullptr;
+  float *c_st = nullptr, *hh = nullptr;  // LSTM cell state [L][chunks][d]; recurrent projection [chunks][G]
+  bf16* h_hl = nullptr;                    // LSTM / GRU: h split into bf16 hi/lo, [L][2][chunks][d]
   uint2* lf = nullptr;
   EncState* es = nullptr;
   DecState* ds = nullptr;
@@ -149,8 +154,12 @@ struct boa_model {
   ~boa_model();
   cudaStream_t stream() const { return own; }
   size_t per_row_bytes() const { return (size_t)40 * d + 4 * (size_t)xpN + 64; }
+  bool is_rnn() const { return backbone == BOA_BACKBONE_LSTM || backbone == BOA_BACKBONE_GRU; }
+  int gates() const { return (backbone == BOA_BACKBONE_LSTM ? 4 : 3) * d; }
   size_t per_chunk_state_bytes() const {
-    return backbone == BOA_BACKBONE_MAMBA ? (size_t)L * 19 * di * 4 : (size_t)L * d * 4;
+    if (backbone == BOA_BACKBONE_MAMBA) return (size_t)L * 19 * di * 4;
+    if (is_rnn()) return (size_t)L * d * (backbone == BOA_BACKBONE_LSTM ? 12 : 8) + (size_t)gates() * 4;
+    return (size_t)L * d * 4;
   }
 };
 
@@ -269,6 +278,11 @@ int ensure_work(boa_model* m, size_t rows, size_t chunks, size_t pitch) {
     plan.push_back({(void**)&m->ssm_st, al((size_t)m->L * chunks * 16 * di * 4)});
   } else {
     plan.push_back({(void**)&m->h_st, al((size_t)m->L * chunks * d * 4)});
+    if (m->backbone == BOA_BACKBONE_LSTM) plan.push_back({(void**)&m->c_st, al((size_t)m->L * chunks * d * 4)});
+    if (m->is_rnn()) {
+      plan.push_back({(void**)&m->h_hl, al((size_t)m->L * 2 * chunks * d * 2)});
+      plan.push_back({(void**)&m->hh, al(chunks * (size_t)m->gates() * 4)});
+    }
   }
   for (auto& p : plan) off += p.second;
   void* base = nullptr;
@@ -306,6 +320,10 @@ int reset_states(boa_model* m, int B) {
       BOA_CK(cudaMemsetAsync(m->ssm_st + (size_t)l * cap * 16 * m->di, 0, (size_t)B * 16 * m->di * 4, m->own));
     } else {
       BOA_CK(cudaMemsetAsync(m->h_st + (size_t)l * cap * m->d, 0, (size_t)B * m->d * 4, m->own));
+      if (m->c_st) BOA_CK(cudaMemsetAsync(m->c_st + (size_t)l * cap * m->d, 0, (size_t)B * m->d * 4, m->own));
+      if (m->h_hl)
+        for (int p = 0; p < 2; ++p)
+          BOA_CK(cudaMemsetAsync(m->h_hl + ((size_t)l * 2 + p) * cap * m->d, 0, (size_t)B * m->d * 2, m->own));
     }
   }
   return 0;
@@ -343,6 +361,23 @@ int forward(boa_model* m, const boa::TokenSrc& src, int B, int T, int head_mode,
       a.N = d; a.K = di; a.bias = w.out_b; a.out_hl = m->xn; a.ld_hl = d; a.plane_hl = xn_plane;
       a.ln_w = w.ln2w; a.ln_b = w.ln2b;
       BOA_LAUNCH(PC_OUT_PROJ_LN, boa::gemm_launch(boa::EPI_LN_SPLIT, m->uhl, u_plane, 0, w.out.p, w.out.plane, a, st));
+    } else if (m->is_rnn()) {
+      // ih for all M rows, then per position: hh (one row per chunk) and the gate update
+      const int G = m->gates();
+      const size_t cap = m->chunks_cap;
+      float* hst = m->h_st + (size_t)l * cap * d;
+      float* cst = m->c_st ? m->c_st + (size_t)l * cap * d : nullptr;
+      bf16* hl = m->h_hl + (size_t)l * 2 * cap * d;
+      a.N = G; a.K = d; a.bias = w.ih_b; a.out_f32 = m->xz; a.ld_f32 = G;
+      BOA_LAUNCH(PC_IN_PROJ, boa::gemm_launch(boa::EPI_F32, m->xn, xn_plane, 0, w.ih.p, w.ih.plane, a, st));
+      for (int t = 0; t < T; ++t) {
+        boa::GemmArgs r{};
+        r.M = B; r.N = G; r.K = d; r.bias = w.hh_b; r.out_f32 = m->hh; r.ld_f32 = G;
+        BOA_LAUNCH(PC_X_PROJ, boa::gemm_launch(boa::EPI_F32, hl, (long long)cap * d, 0, w.hh.p, w.hh.plane, r, st));
+        BOA_LAUNCH(PC_SCAN, boa::launch_rnn_gates(m->backbone == BOA_BACKBONE_LSTM, m->xz, m->hh, d, t, T, hst, cst,
+                                                  hl, (long long)cap * d, m->u, B, st));
+      }
+      BOA_LAUNCH(PC_OTHER, boa::launch_add_ln(m->x, m->u, d, m->xn, xn_plane, w.ln2w, w.ln2b, M, st));
     } else {
       float* hst = m->h_st + (size_t)l * m->chunks_cap * d;
       a.N = 2 * d; a.K = d; a.bias = w.zh_b; a.out_f32 = m->xz; a.ld_f32 = 2 * d;
@@ -479,8 +514,8 @@ const char* boa_last_error(const boa_model* h) { return h ? h->err.c_str() : g_l
 int boa_model_load(const char* path, int backbone, int d, int nl, int device, boa_model** out) {
   if (!out) return fail(nullptr, BOA_E_INVALID, "out is NULL");
   *out = nullptr;
-  if (backbone != BOA_BACKBONE_MAMBA && backbone != BOA_BACKBONE_MINGRU)
-    return fail(nullptr, BOA_E_INVALID, "backbone must be mamba (0) or mingru (3)");
+  if (backbone < BOA_BACKBONE_MAMBA || backbone > BOA_BACKBONE_MINGRU)
+    return fail(nullptr, BOA_E_INVALID, "backbone must be mamba (0), lstm (1), gru (2) or mingru (3)");
   if (!(d == 64 || d == 128 || d == 256 || d == 512) || nl <= 0 || nl > 256)
     return fail(nullptr, BOA_E_INVALID, "d_model must be 64, 128, 256 or 512 and n_layers in 1..256");
   FileReader R;
@@ -522,7 +557,7 @@ int boa_model_load(const char* path, int backbone, int d, int nl, int device, bo
   std::vector<HostHL> hls;                 // bf16 pairs in upload order
   std::vector<float> emb = R.vec((size_t)256 * d);
   struct LIdx { int ln1w, ln1b, ln2w, ln2b, ff1_b, ff2_b, in_b, conv_w, conv_b, dt_w, dt_b, negA, Dv, out_b, zh_b;
-                int ff1, ff2, in, xp, out, zh; };
+                int ff1, ff2, in, xp, out, zh, ih, ih_b, hh, hh_b; };
   std::vector<LIdx> li(nl);
   auto addf = [&](std::vector<float> v) { f32s.push_back(std::move(v)); return (int)f32s.size() - 1; };
   auto addh = [&](HostHL h) { hls.push_back(std::move(h)); return (int)hls.size() - 1; };
@@ -545,6 +580,13 @@ int boa_model_load(const char* path, int backbone, int d, int nl, int device, bo
       x.Dv = addf(R.vec(di));
       x.out = addh(make_hl(R.vec((size_t)d * di), d, di, d));
       x.out_b = addf(R.vec(d));
+    } else if (backbone == BOA_BACKBONE_LSTM || backbone == BOA_BACKBONE_GRU) {
+      // w_ih [G][d], b_ih, w_hh [G][d], b_hh (boa_gpu.hpp:413-419, :526-532)
+      const int G = (backbone == BOA_BACKBONE_LSTM ? 4 : 3) * d;
+      x.ih = addh(make_hl(R.vec((size_t)G * d), G, d, G));
+      x.ih_b = addf(R.vec(G));
+      x.hh = addh(make_hl(R.vec((size_t)G * d), G, d, G));
+      x.hh_b = addf(R.vec(G));
     } else {
       std::vector<float> wz = R.vec((size_t)d * d), bz = R.vec(d), wh = R.vec((size_t)d * d), bh = R.vec(d);
       wz.insert(wz.end(), wh.begin(), wh.end());
@@ -610,6 +652,8 @@ int boa_model_load(const char* path, int backbone, int d, int nl, int device, bo
       w.in = hp[x.in]; w.in_b = fp[x.in_b]; w.conv_w = fp[x.conv_w]; w.conv_b = fp[x.conv_b];
       w.xp = hp[x.xp]; w.dt_w = fp[x.dt_w]; w.dt_b = fp[x.dt_b]; w.negA = fp[x.negA]; w.Dv = fp[x.Dv];
       w.out = hp[x.out]; w.out_b = fp[x.out_b];
+    } else if (backbone == BOA_BACKBONE_LSTM || backbone == BOA_BACKBONE_GRU) {
+      w.ih = hp[x.ih]; w.ih_b = fp[x.ih_b]; w.hh = hp[x.hh]; w.hh_b = fp[x.hh_b];
     } else {
       w.zh = hp[x.zh]; w.zh_b = fp[x.zh_b];
     }

@@ -60,6 +60,14 @@ def weight_tensors(backbone: str, d_model: int, n_layers: int):
             yield (m + "linear_z.bias", (d,), "rand")
             yield (m + "linear_h.weight", (d, d), "rand")
             yield (m + "linear_h.bias", (d,), "rand")
+        elif BACKBONES[backbone] in (1, 2):
+            # convert_boa_weights.py export_lstm_block / export_gru_block order
+            g = (4 if BACKBONES[backbone] == 1 else 3) * d
+            m = p + ("lstm." if BACKBONES[backbone] == 1 else "gru.")
+            yield (m + "weight_ih_l0", (g, d), "rand")
+            yield (m + "bias_ih_l0", (g,), "rand")
+            yield (m + "weight_hh_l0", (g, d), "rand")
+            yield (m + "bias_hh_l0", (g,), "rand")
         else:
             raise ValueError(f"backbone {backbone!r} is not on this path")
         yield (p + "ln2.weight", (d,), "one")
@@ -107,8 +115,8 @@ def write_weights(path: str, tensors, fp16: bool = False) -> int:
 
 
 def write_random_weights(path: str, backbone: str = "mamba", d_model: int = 256,
-                         n_layers: int = 8, seed: int = 0, fp16: bool = False) -> int:
-    return write_weights(path, random_weights(backbone, d_model, n_layers, seed), fp16=fp16)
+                         n_layers: int = 8, seed: int = 0, fp16: bool = False, std: float = 0.02) -> int:
+    return write_weights(path, random_weights(backbone, d_model, n_layers, seed, std=std), fp16=fp16)
 
 
 def particle_stream(n_bytes: int, seed: int) -> bytes:

@@ -33,7 +33,9 @@ extern "C" {
 #define BOA_E_NOMEM (-6)     /* device allocation failed */
 
 #define BOA_BACKBONE_MAMBA 0 /* gemm_gpu.hpp BackboneType: mamba (mambav1 blocks) */
-#define BOA_BACKBONE_MINGRU 3
+#define BOA_BACKBONE_LSTM 1   /* LSTMBlockGPU (boa_gpu.hpp:365-502) */
+#define BOA_BACKBONE_GRU 2    /* GRUBlockGPU (boa_gpu.hpp:504-600) */
+#define BOA_BACKBONE_MINGRU 3 /* MinGRUBlockGPU (boa_gpu.hpp:605-694) */
 
 typedef struct boa_model boa_model;
 

@@ -141,8 +141,10 @@ struct MambaW {
   std::vector<float> ln1w, ln1b, in_t, in_b, conv_w, conv_b, xp_t, dt_t, dt_b, negA, D, out_t, out_b;
 };
 struct GruW { std::vector<float> wz_t, bz, wh_t, bh; };
+// LSTM (G = 4d, gates i f g o) and GRU (G = 3d, gates r z n): W_ih / W_hh transposed to [d][G]
+struct RnnW { std::vector<float> wih_t, bih, whh_t, bhh; };
 struct BlockW {
-  MambaW m; GruW g;
+  MambaW m; GruW g; RnnW rnn;
   std::vector<float> ln1w, ln1b, ln2w, ln2b, ff1_t, ff1_b, ff2_t, ff2_b;
 };
 
@@ -158,13 +160,14 @@ struct Model {
 // ----------------------------------------------------------------------------
 struct State {
   // mamba: conv [L][di][3] (last three inputs, oldest first), ssm [L][di][16]
-  std::vector<float> conv, ssm, h;  // h: minGRU [L][d]
+  std::vector<float> conv, ssm, h, c;  // h: minGRU / LSTM / GRU [L][d]; c: LSTM cell [L][d]
   void init(const Model& M) {
     if (M.backbone == MAMBA) {
       conv.assign((size_t)M.L * M.di * 3, 0.f);
       ssm.assign((size_t)M.L * M.di * M.dst, 0.f);
     } else {
       h.assign((size_t)M.L * M.d, 0.f);
+      if (M.backbone == LSTM) c.assign((size_t)M.L * M.d, 0.f);
     }
   }
 };
@@ -259,6 +262,43 @@ void mingru_forward(const Model& M, const GruW& W, float* h, const float* xin, f
   }
 }
 
+// LSTM / GRU backbone over T tokens of one chunk (boa_gpu.hpp:466-501,
+// :567-582).  ih = x W_ih^T + b_ih for all T rows at once, then per token
+// hh = h W_hh^T + b_hh and the fused gate update of rnn_kernels.cu:16-161
+// (GPU_REPRO_MATH branch: repro_sigmoid / repro_tanh, products and sums
+// rounded separately).
+void rnn_forward(const Model& M, const RnnW& W, float* h, float* c, const float* xin, float* xout,
+                 int T, Scratch& s) {
+  const int d = M.d, G = (M.backbone == LSTM ? 4 : 3) * d;
+  s.xz.resize((size_t)T * G + G);
+  float* ih = s.xz.data();
+  float* hh = s.xz.data() + (size_t)T * G;
+  gemm(xin, d, W.wih_t.data(), W.bih.data(), ih, G, T, d, G, ACT_NONE);
+  for (int t = 0; t < T; ++t) {
+    gemm(h, d, W.whh_t.data(), W.bhh.data(), hh, G, 1, d, G, ACT_NONE);
+    const float* a = ih + (size_t)t * G;
+    for (int j = 0; j < d; ++j) {
+      if (M.backbone == LSTM) {
+        const float iv = sigmoidf_(a[j] + hh[j]);
+        const float fv = sigmoidf_(a[d + j] + hh[d + j]);
+        const float gv = tanh_ref(a[2 * d + j] + hh[2 * d + j]);
+        const float ov = sigmoidf_(a[3 * d + j] + hh[3 * d + j]);
+        const float fc = fv * c[j], ig = iv * gv;
+        c[j] = fc + ig;
+        h[j] = ov * tanh_ref(c[j]);
+      } else {
+        const float r = sigmoidf_(a[j] + hh[j]);
+        const float z = sigmoidf_(a[d + j] + hh[d + j]);
+        const float rn = r * hh[2 * d + j];
+        const float n = tanh_ref(a[2 * d + j] + rn);
+        const float p = (1.0f - z) * n, q = z * h[j];
+        h[j] = p + q;
+      }
+    }
+    std::memcpy(xout + (size_t)t * d, h, d * sizeof(float));
+  }
+}
+
 // Full predictor over T tokens of one chunk (boa_gpu.hpp:1081-1102 / 892-928).
 void predictor_forward(const Model& M, State& st, const uint8_t* tok, int T, float* logits, Scratch& s) {
   const int d = M.d;
@@ -280,7 +320,11 @@ void predictor_forward(const Model& M, State& st, const uint8_t* tok, int T, flo
     } else {
       // x = x + minGRU(LN1 x); x = x + FF(LN2 x)  (boa_gpu.hpp:903-927)
       layernorm(s.x.data(), s.xn.data(), B.ln1w.data(), B.ln1b.data(), T, d);
-      mingru_forward(M, B.g, st.h.data() + (size_t)l * d, s.xn.data(), s.mo.data(), T, s);
+      if (M.backbone == MINGRU)
+        mingru_forward(M, B.g, st.h.data() + (size_t)l * d, s.xn.data(), s.mo.data(), T, s);
+      else
+        rnn_forward(M, B.rnn, st.h.data() + (size_t)l * d,
+                    M.backbone == LSTM ? st.c.data() + (size_t)l * d : nullptr, s.xn.data(), s.mo.data(), T, s);
       for (size_t i = 0; i < (size_t)T * d; ++i) s.x[i] = s.mo[i] + s.x[i];
       layernorm(s.x.data(), s.xn.data(), B.ln2w.data(), B.ln2b.data(), T, d);
       gemm(s.xn.data(), d, B.ff1_t.data(), B.ff1_b.data(), s.ff.data(), 4 * d, T, d, 4 * d, ACT_GELU);
@@ -466,7 +510,7 @@ Model* load_model(const char* path, int backbone, int d, int nl) {
   buf.resize(sz > 0 ? sz : 0);
   if (sz > 0 && std::fread(buf.data(), 1, sz, f) != (size_t)sz) { std::fclose(f); g_err = "short read"; return nullptr; }
   std::fclose(f);
-  if (backbone != MAMBA && backbone != MINGRU) { g_err = "oracle supports mamba and mingru backbones"; return nullptr; }
+  if (backbone < MAMBA || backbone > MINGRU) { g_err = "backbone must be 0 (mamba), 1 (lstm), 2 (gru) or 3 (mingru)"; return nullptr; }
   if (d <= 0 || nl <= 0 || d % 16 != 0) { g_err = "bad model dims"; return nullptr; }
   Reader R{buf.data(), buf.size()};
   if (buf.size() >= 4 && buf[0] == 'B' && buf[1] == 'O' && buf[2] == 'A') { R.fp16 = buf[3] == 1; R.off = 4; }
@@ -493,6 +537,11 @@ Model* load_model(const char* path, int backbone, int d, int nl) {
       W.D = R.vec(di);
       W.out_t = transpose(R.vec((size_t)d * di), d, di);
       W.out_b = R.vec(d);
+    } else if (backbone == LSTM || backbone == GRU) {  // boa_gpu.hpp:413-419, :526-532
+      const int G = (backbone == LSTM ? 4 : 3) * d;
+      RnnW& W = B.rnn;
+      W.wih_t = transpose(R.vec((size_t)G * d), G, d); W.bih = R.vec(G);
+      W.whh_t = transpose(R.vec((size_t)G * d), G, d); W.bhh = R.vec(G);
     } else {  // boa_gpu.hpp:643-648
       GruW& G = B.g;
       G.wz_t = transpose(R.vec((size_t)d * d), d, d); G.bz = R.vec(d);

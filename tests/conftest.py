@@ -75,11 +75,11 @@ def weights(boa, wdir):
     """Factory: path of a random-init weight file (cached per config)."""
     cache = {}
 
-    def make(backbone="mamba", d=256, L=8, seed=0):
-        key = (backbone, d, L, seed)
+    def make(backbone="mamba", d=256, L=8, seed=0, std=0.02):
+        key = (backbone, d, L, seed, std)
         if key not in cache:
-            p = str(wdir / f"w_{backbone}_{d}_{L}_{seed}.bin")
-            boa.synth.write_random_weights(p, backbone, d, L, seed)
+            p = str(wdir / f"w_{backbone}_{d}_{L}_{seed}_{std}.bin")
+            boa.synth.write_random_weights(p, backbone, d, L, seed, std=std)
             cache[key] = p
         return cache[key]
     return make

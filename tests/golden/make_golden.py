@@ -37,8 +37,16 @@ spec.loader.exec_module(synth)
 
 EXACT = dict(d_model=64, n_layers=1, seed=7, support=list(range(0, 256, 5)) + [255],
              n_bytes=4001, data_seed=11, chunk=1000, batch=8, p_out=0.05)
+# "backbone" defaults to mamba and "std" (weight init) to 0.02; the RNN
+# backbones use std 0.1 so that their gates leave the linear region.
 LOGIT_CFGS = [dict(name="d64L2", d_model=64, n_layers=2, seed=3, B=3, T=40, tok_seed=5),
-              dict(name="d256L8", d_model=256, n_layers=8, seed=0, B=2, T=48, tok_seed=6)]
+              dict(name="d256L8", d_model=256, n_layers=8, seed=0, B=2, T=48, tok_seed=6),
+              dict(name="mingru_d64L2", backbone="mingru", std=0.1, d_model=64, n_layers=2, seed=3, B=3, T=40,
+                   tok_seed=5),
+              dict(name="lstm_d64L2", backbone="lstm", std=0.1, d_model=64, n_layers=2, seed=3, B=3, T=40,
+                   tok_seed=5),
+              dict(name="gru_d64L2", backbone="gru", std=0.1, d_model=64, n_layers=2, seed=3, B=3, T=40,
+                   tok_seed=5)]
 RAND = dict(d_model=256, n_layers=8, seed=0, n_bytes=65536, data_seed=1, chunk=4096, batch=16)
 
 
@@ -72,14 +80,15 @@ def main(out_dir):
 
     for c in LOGIT_CFGS:
         w = os.path.join(tmp, f"w_{c['name']}.bin")
-        synth.write_random_weights(w, "mamba", c["d_model"], c["n_layers"], c["seed"])
+        bb = c.get("backbone", "mamba")
+        synth.write_random_weights(w, bb, c["d_model"], c["n_layers"], c["seed"], std=c.get("std", 0.02))
         tok = np.random.default_rng(c["tok_seed"]).integers(0, 256, (c["B"], c["T"]), dtype=np.uint8)
         tf = os.path.join(tmp, "tok.u8")
         tok.tofile(tf)
         res = {}
         for mode in ("chunk", "step"):
             of = os.path.join(tmp, f"lg_{mode}.f32")
-            run([os.path.join(REF, "ref_logits"), w, "mamba", str(c["d_model"]), str(c["n_layers"]),
+            run([os.path.join(REF, "ref_logits"), w, bb, str(c["d_model"]), str(c["n_layers"]),
                  tf, str(c["B"]), str(c["T"]), mode, of])
             res[mode] = np.fromfile(of, np.float32).reshape(c["B"], c["T"], 256)
         np.savez_compressed(os.path.join(out_dir, f"ref_logits_{c['name']}.npz"),

@@ -45,7 +45,10 @@ def test_load_rejects_bad_arguments(boa, weights, tmp_path):
         boa.Model(weights("mamba", 64, 2, 3), "mamba", 64, 3)  # dims do not match the file
     assert e.value.code == boa.BOA_E_FORMAT
     with pytest.raises(boa.BoaError) as e:
-        boa.Model(weights("mamba", 64, 2, 3), "lstm", 64, 2)
+        boa.Model(weights("mamba", 64, 2, 3), "lstm", 64, 2)  # an LSTM file of these dims is larger
+    assert e.value.code == boa.BOA_E_FORMAT
+    with pytest.raises(boa.BoaError) as e:
+        boa.Model(weights("mamba", 64, 2, 3), 7, 64, 2)  # no such backbone
     assert e.value.code == boa.BOA_E_INVALID
     p = tmp_path / "bad_magic.bin"
     p.write_bytes(b"BOA\x07" + b"\0" * 64)

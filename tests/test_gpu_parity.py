@@ -71,11 +71,13 @@ def test_cdf_general_logits_close(boa, oracle, m64):
 
 
 # ---------------------------------------------------------------- model logits
-@pytest.mark.parametrize("cfg", ["d64L2", "d256L8"])
+@pytest.mark.parametrize("cfg", ["d64L2", "d256L8", "mingru_d64L2", "lstm_d64L2", "gru_d64L2"])
 def test_logits_vs_reference_golden(boa, oracle, manifest, weights, cfg):
     c = next(x for x in manifest["logits"] if x["name"] == cfg)
     z = np.load(f"{GOLDEN}/ref_logits_{cfg}.npz")
-    m = boa.Model(weights("mamba", c["d_model"], c["n_layers"], c["seed"]), "mamba", c["d_model"], c["n_layers"])
+    bb = c.get("backbone", "mamba")
+    m = boa.Model(weights(bb, c["d_model"], c["n_layers"], c["seed"], c.get("std", 0.02)), bb, c["d_model"],
+                  c["n_layers"])
     for mode in (0, 1):
         lg = m.logits(z["tokens"], mode)
         ref = z["chunk"]
@@ -179,6 +181,24 @@ def test_mingru_roundtrip_and_logits(boa, oracle, weights):
     _roundtrip(boa, m, data, 1024)
 
 
+@pytest.mark.parametrize("backbone,d", [("lstm", 64), ("gru", 64), ("lstm", 256), ("gru", 128), ("gru", 512)])
+def test_rnn_backbone_logits_and_roundtrip(boa, oracle, weights, backbone, d):
+    """LSTM / GRU blocks (boa_gpu.hpp:365-600): logits against the oracle in
+    both the tile form and the one-position step form, bitwise agreement of
+    the two forms, and a byte-exact round trip with several tiles per chunk."""
+    p = weights(backbone, d, 2, 4, 0.1)
+    m = boa.Model(p, backbone, d, 2)
+    tok = np.random.default_rng(13).integers(0, 256, (3, 37), dtype=np.uint8)
+    ref = oracle.OracleModel(p, boa.BACKBONES[backbone], d, 2).logits(tok, 0)
+    lg = m.logits(tok, 0)
+    assert np.abs(lg - ref).max() <= LOGIT_RTOL * np.abs(ref).max()
+    assert np.array_equal(lg, m.logits(tok, 1))
+    data = boa.synth.particle_stream(4000, 6)
+    _roundtrip(boa, m, data, 900)
+    m.set_batch(2, 64)
+    _roundtrip(boa, m, data[:2701], 900)
+
+
 def test_cli_roundtrip(boa, weights, tmp_path):
     data = boa.synth.particle_stream(20000, 5)
     src, enc, dec = tmp_path / "in.bin", tmp_path / "x.boa", tmp_path / "out.bin"
@@ -188,6 +208,20 @@ def test_cli_roundtrip(boa, weights, tmp_path):
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
     r = subprocess.run([boa.CLI_PATH, "decompress", w, str(enc), str(dec), "64", "2"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    assert dec.read_bytes() == data
+
+
+def test_cli_rnn_backbone_roundtrip(boa, weights, tmp_path):
+    data = boa.synth.particle_stream(5000, 8)
+    src, enc, dec = tmp_path / "in.bin", tmp_path / "x.boa", tmp_path / "out.bin"
+    src.write_bytes(data)
+    w = weights("gru", 64, 2, 4, 0.1)
+    r = subprocess.run([boa.CLI_PATH, "compress", w, str(src), str(enc), "64", "2", "--backbone", "gru",
+                        "--chunk-size", "1200"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([boa.CLI_PATH, "decompress", w, str(enc), str(dec), "64", "2", "--backbone", "gru"],
+                       capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
     assert dec.read_bytes() == data
 

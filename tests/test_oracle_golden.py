@@ -6,14 +6,18 @@ import pytest
 from conftest import GOLDEN, dirichlet_cdfs
 
 
-@pytest.mark.parametrize("cfg", ["d64L2", "d256L8"])
+LOGIT_CFGS = ["d64L2", "d256L8", "mingru_d64L2", "lstm_d64L2", "gru_d64L2"]
+
+
+@pytest.mark.parametrize("cfg", LOGIT_CFGS)
 @pytest.mark.parametrize("mode", [0, 1])
 def test_oracle_logits_match_reference_gpu(oracle, boa, manifest, wdir, cfg, mode):
     c = next(x for x in manifest["logits"] if x["name"] == cfg)
     z = np.load(f"{GOLDEN}/ref_logits_{cfg}.npz")
     p = str(wdir / f"g_{cfg}.bin")
-    boa.synth.write_random_weights(p, "mamba", c["d_model"], c["n_layers"], c["seed"])
-    m = oracle.OracleModel(p, 0, c["d_model"], c["n_layers"])
+    bb = c.get("backbone", "mamba")
+    boa.synth.write_random_weights(p, bb, c["d_model"], c["n_layers"], c["seed"], std=c.get("std", 0.02))
+    m = oracle.OracleModel(p, boa.BACKBONES[bb], c["d_model"], c["n_layers"])
     lg = m.logits(z["tokens"], mode)
     ref = z["chunk" if mode == 0 else "step"]
     # the oracle uses libm exp/log, the reference CUDA's: agree to ~1e-6
@@ -104,3 +108,13 @@ def test_oracle_warm_start_roundtrip(oracle, boa, weights):
     fb1, st1 = m.compress(data, 300, warm=12)  # one chunk per lane == plain
     fb0, st0 = m.compress(data, 300)
     assert all(np.array_equal(a, b) for a, b in zip(st0, st1))
+
+
+@pytest.mark.parametrize("backbone", ["lstm", "gru"])
+def test_oracle_rnn_roundtrip(oracle, boa, weights, backbone):
+    m = oracle.OracleModel(weights(backbone, 64, 2, 4, 0.1), boa.BACKBONES[backbone], 64, 2)
+    data = bytes(np.random.default_rng(6).integers(0, 256, 700, dtype=np.uint8))
+    fb, st = m.compress(data, 300)
+    assert m.decompress(fb, st, len(data), 300) == data
+    tok = np.frombuffer(data[:64], np.uint8).reshape(2, 32)
+    assert np.array_equal(m.logits(tok, 0), m.logits(tok, 1))
