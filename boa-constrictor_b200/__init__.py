@@ -15,6 +15,7 @@ The directory name contains a hyphen, so load it by path::
 from __future__ import annotations
 
 import ctypes as C
+import hashlib
 import os
 import subprocess
 
@@ -34,6 +35,7 @@ PROF_CLASSES = 12
 
 _u8p, _u32p, _u64p, _f32p = (C.POINTER(C.c_uint8), C.POINTER(C.c_uint32), C.POINTER(C.c_uint64),
                              C.POINTER(C.c_float))
+_i32p = C.POINTER(C.c_int32)
 
 
 class BoaError(RuntimeError):
@@ -51,7 +53,8 @@ def build(jobs: int = 8) -> str:
 class boa2_info(C.Structure):
     _fields_ = [("total_size", C.c_uint64), ("chunk_len", C.c_uint32), ("n_chunks", C.c_uint32),
                 ("last_chunk_len", C.c_uint32), ("flags", C.c_uint32), ("interleave_batch", C.c_uint32),
-                ("index_version", C.c_uint32), ("payload_offset", C.c_uint64), ("payload_bytes", C.c_uint64)]
+                ("index_version", C.c_uint32), ("payload_offset", C.c_uint64), ("payload_bytes", C.c_uint64),
+                ("fp_len", C.c_uint32), ("fp", C.c_uint8 * 255)]
 
 
 _LIB = None
@@ -87,7 +90,18 @@ SIGNATURES = {
     "boa_cdf_from_logits": (C.c_int, [C.c_void_p, _f32p, C.c_int, C.c_float, _u32p]),
     "boa_boa2_build": (C.c_int, [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _u8p,
                                  _u64p, _u8p, _u8p, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "boa_boa2_build_fp": (C.c_int, [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _u8p, C.c_uint32,
+                                    _u8p, _u64p, _u8p, _u8p, C.c_size_t, C.POINTER(C.c_size_t)]),
     "boa_boa2_parse": (C.c_int, [_u8p, C.c_size_t, C.POINTER(boa2_info), _u8p, _u64p, _u64p]),
+    "boa_pyrc_create": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
+    "boa_pyrc_free": (None, [C.c_void_p]),
+    "boa_pyrc_last_error": (C.c_char_p, [C.c_void_p]),
+    "boa_pyrc_encode_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "boa_pyrc_finalize": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "boa_pyrc_read": (C.c_int, [C.c_void_p, _u32p, _i32p, C.c_void_p]),
+    "boa_pyrc_load": (C.c_int, [C.c_void_p, _u32p, _i32p, C.c_void_p]),
+    "boa_pyrc_init_decoder": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "boa_pyrc_decode_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
 }
 
 
@@ -258,8 +272,21 @@ class Model:
 
 
 # -------------------------------------------------------------------- container
-def boa2_build(total_size: int, chunk_len: int, first_bytes, sizes_words, payload_words, warm_start: int = 0) -> bytes:
-    """warm_start = interleave batch W of a warm-start container (flags bit0), 0 = off."""
+PYTHON_MODEL_CLASS = "BoaBytePredictor"  # the nn.Module that model.BoaConstrictor() returns (model.py:1754)
+
+
+def python_fingerprint(class_name: str = PYTHON_MODEL_CLASS) -> bytes:
+    """The fingerprint field Python BoaFile writes: blake2s of the model's class
+    name, 16-byte digest (boa.py:107-109)."""
+    return hashlib.blake2s(class_name.encode(), digest_size=16).digest()
+
+
+def boa2_build(total_size: int, chunk_len: int, first_bytes, sizes_words, payload_words, warm_start: int = 0,
+               fingerprint: bytes | None = None) -> bytes:
+    """warm_start = interleave batch W of a warm-start container (flags bit0), 0 = off.
+    fingerprint: bytes stored verbatim in the fingerprint field (e.g.
+    python_fingerprint() for a file in the Python BoaFile dialect); None keeps
+    the C++ writer's rule."""
     n = len(sizes_words)
     last = total_size - (n - 1) * chunk_len if n > 1 else total_size
     fb = np.ascontiguousarray(first_bytes, np.uint8)
@@ -273,11 +300,19 @@ def boa2_build(total_size: int, chunk_len: int, first_bytes, sizes_words, payloa
         sb = np.zeros(1, np.uint64)
     ln = C.c_size_t()
     flags = 1 if warm_start else 0
-    _check(lib().boa_boa2_build(total_size, chunk_len, n, last, flags, warm_start, _p(fb, _u8p), _p(sb, _u64p),
-                                _p(pay, _u8p), None, 0, C.byref(ln)))
+    if fingerprint is None:
+        def call(out, cap):
+            return lib().boa_boa2_build(total_size, chunk_len, n, last, flags, warm_start, _p(fb, _u8p),
+                                        _p(sb, _u64p), _p(pay, _u8p), out, cap, C.byref(ln))
+    else:
+        fp = np.frombuffer(bytes(fingerprint) or b"\0", np.uint8).copy()
+
+        def call(out, cap):
+            return lib().boa_boa2_build_fp(total_size, chunk_len, n, last, flags, _p(fp, _u8p), len(fingerprint),
+                                           _p(fb, _u8p), _p(sb, _u64p), _p(pay, _u8p), out, cap, C.byref(ln))
+    _check(call(None, 0))
     buf = np.zeros(ln.value, np.uint8)
-    _check(lib().boa_boa2_build(total_size, chunk_len, n, last, flags, warm_start, _p(fb, _u8p), _p(sb, _u64p),
-                                _p(pay, _u8p), _p(buf, _u8p), buf.size, C.byref(ln)))
+    _check(call(_p(buf, _u8p), buf.size))
     return buf.tobytes()
 
 
@@ -297,4 +332,5 @@ def boa2_parse(blob: bytes) -> dict:
     streams = [blob[base + int(o): base + int(o) + int(l)] for o, l in zip(off[:n], ln[:n])]
     return dict(total_size=info.total_size, chunk_len=info.chunk_len, n_chunks=n,
                 last_chunk_len=info.last_chunk_len, flags=info.flags, interleave_batch=info.interleave_batch,
-                index_version=info.index_version, first_bytes=fb[:n].copy(), streams=streams)
+                index_version=info.index_version, first_bytes=fb[:n].copy(), streams=streams,
+                fingerprint=bytes(info.fp[:info.fp_len]))

@@ -8,3 +8,4 @@
 #include "runtime.cpp"
 #include "container.cpp"
 #include "noalloc.cu"
+#include "pyrc.cu"

@@ -70,7 +70,17 @@ extern "C" {
 int boa_boa2_build(uint64_t total, uint32_t chunk_len, uint32_t n_chunks, uint32_t last_len, uint32_t flags,
                    uint32_t interleave, const uint8_t* first_bytes, const uint64_t* stream_bytes,
                    const uint8_t* payload, uint8_t* buf, size_t cap, size_t* len_out) {
+  uint8_t fp[4];
+  std::memcpy(fp, &interleave, 4);
+  return boa_boa2_build_fp(total, chunk_len, n_chunks, last_len, flags, fp, (flags & 1u) ? 4 : 0, first_bytes,
+                           stream_bytes, payload, buf, cap, len_out);
+}
+
+int boa_boa2_build_fp(uint64_t total, uint32_t chunk_len, uint32_t n_chunks, uint32_t last_len, uint32_t flags,
+                      const uint8_t* fp, uint32_t fp_len, const uint8_t* first_bytes, const uint64_t* stream_bytes,
+                      const uint8_t* payload, uint8_t* buf, size_t cap, size_t* len_out) {
   if (!len_out || (n_chunks && (!first_bytes || !stream_bytes))) return BOA_E_INVALID;
+  if (fp_len > 255 || (fp_len && !fp)) return BOA_E_INVALID;
   uint64_t pay = 0;
   for (uint32_t i = 0; i < n_chunks; ++i) pay += stream_bytes[i];
   if (pay && !payload) return BOA_E_INVALID;
@@ -82,8 +92,8 @@ int boa_boa2_build(uint64_t total, uint32_t chunk_len, uint32_t n_chunks, uint32
   put<uint32_t>(head, chunk_len);
   put<uint32_t>(head, n_chunks);
   put<uint32_t>(head, last_len);
-  if (flags & 1u) { head.push_back(4); put<uint32_t>(head, interleave); }
-  else head.push_back(0);
+  head.push_back((uint8_t)fp_len);
+  head.insert(head.end(), fp, fp + fp_len);
   idx.insert(idx.end(), {'I', 'D', 'X', '2'});
   idx.insert(idx.end(), first_bytes, first_bytes + n_chunks);
   for (uint32_t i = 0; i < n_chunks; ++i) put_uvarint(idx, stream_bytes[i]);
@@ -116,6 +126,8 @@ int boa_boa2_parse(const uint8_t* buf, size_t len, boa2_info* info, uint8_t* fir
   const uint8_t fp_len = buf[p++];
   if (p + fp_len > len) return BOA_E_FORMAT;
   if ((I.flags & 1u) && fp_len >= 4) I.interleave_batch = get<uint32_t>(buf + p);
+  I.fp_len = fp_len;
+  std::memcpy(I.fp, buf + p, fp_len);
   p += fp_len;
   I.payload_offset = p;
   // backward scan for the index marker (boa.cpp:218-225)

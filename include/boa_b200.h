@@ -172,17 +172,65 @@ int boa_boa2_build(uint64_t total_size, uint32_t chunk_len, uint32_t n_chunks, u
                    uint32_t flags, uint32_t interleave_batch, const uint8_t* first_bytes,
                    const uint64_t* stream_bytes, const uint8_t* payload, uint8_t* buf, size_t cap,
                    size_t* len_out);
+/* Same, with the fingerprint field given verbatim (fp_len <= 255 bytes): the
+ * Python BoaFile writer stores blake2s(model class name, digest_size=16)
+ * there with flags 0 (boa.py:107-131, :226-240); the C++ writer stores the
+ * 4-byte interleave batch under warm start or nothing (boa.cpp:230-237). */
+int boa_boa2_build_fp(uint64_t total_size, uint32_t chunk_len, uint32_t n_chunks, uint32_t last_chunk_len,
+                      uint32_t flags, const uint8_t* fp, uint32_t fp_len, const uint8_t* first_bytes,
+                      const uint64_t* stream_bytes, const uint8_t* payload, uint8_t* buf, size_t cap,
+                      size_t* len_out);
 typedef struct boa2_info {
   uint64_t total_size;
   uint32_t chunk_len, n_chunks, last_chunk_len, flags, interleave_batch;
   uint32_t index_version; /* 1 or 2 */
   uint64_t payload_offset, payload_bytes;
+  uint32_t fp_len;        /* fingerprint field as stored */
+  uint8_t fp[255];
 } boa2_info;
 /* Parses and validates (magic, version, index, CRC-32, ranges).  first_bytes,
  * offsets and lengths (bytes, relative to the payload) may be NULL to query
  * info only; otherwise they need n_chunks entries. */
 int boa_boa2_parse(const uint8_t* buf, size_t len, boa2_info* info, uint8_t* first_bytes, uint64_t* offsets,
                    uint64_t* lengths);
+
+/* ---- the Python codec's batch coder (gpu_range_coder.py:57-298) ---------
+ * Replaces gpu_range_coder.gpu.queue.RangeCoderBatch, which codec.py's
+ * compress_GPU / decompress_GPU (codec.py:11-151) call once per position.
+ * Each step takes one fp32 probability row per stream ([n_streams][vocab],
+ * device memory), quantises it with build_cdf_fast (cdf[i] = (u32)(P_i *
+ * (2^24 - vocab) / P_vocab) + i, P_i the left-to-right fp64 prefix sum) and
+ * range-codes one symbol with the same 64-bit-state, 32-bit-word coder as
+ * the C++ path.  Streams are bit-for-bit the reference's for equal
+ * probabilities.  One handle per stream batch and device; device buffers
+ * are the handle's, host buffers the caller's.  d_mask (uint8 or bool, may
+ * be NULL) skips streams whose byte is 0; encode also skips symbols outside
+ * [0, vocab), as the reference does.  Work goes on `stream` (NULL = legacy
+ * default stream) without synchronising, except read / load. */
+typedef struct boa_pyrc boa_pyrc;
+/* RangeCoderBatch(N, K, pitch) (:217-237); vocab <= 1024, as the reference's
+ * 1025-entry CDF array.  Words are zeroed and encoder states reset. */
+int boa_pyrc_create(int n_streams, int vocab, int pitch_words, int device, boa_pyrc** out);
+void boa_pyrc_free(boa_pyrc* h);
+const char* boa_pyrc_last_error(const boa_pyrc* h);
+/* encode_step_from_device (:262-269): symbols int32 [n_streams] */
+int boa_pyrc_encode_step(boa_pyrc* h, const int32_t* d_symbols, const float* d_probs, const uint8_t* d_mask,
+                         void* stream);
+/* finalize (:270-274) */
+int boa_pyrc_finalize(boa_pyrc* h, void* stream);
+/* get_compressed_host / get_sizes_host (:241-245, :275-287): sizes [n_streams]
+ * and, when words_host is not NULL, the [n_streams][pitch_words] buffer.
+ * BOA_E_DEVICE if a stream outgrew pitch_words (the reference writes past
+ * its buffer there). */
+int boa_pyrc_read(boa_pyrc* h, uint32_t* words_host, int32_t* sizes_host, void* stream);
+/* load_compressed_from_host (:224-240): [n_streams][pitch_words] words and
+ * the word count of each stream (<= pitch_words). */
+int boa_pyrc_load(boa_pyrc* h, const uint32_t* words_host, const int32_t* sizes_host, void* stream);
+/* init_decoder_from_current_bytes (:288-292) */
+int boa_pyrc_init_decoder(boa_pyrc* h, void* stream);
+/* decode_step_to_device (:293-300): symbols int32 [n_streams] */
+int boa_pyrc_decode_step(boa_pyrc* h, const float* d_probs, int32_t* d_out_symbols, const uint8_t* d_mask,
+                         void* stream);
 
 #ifdef __cplusplus
 }

@@ -8,6 +8,8 @@ and read by read_boa2 (boa.cpp:190-277):
     u32 chunk_len | u32 n_chunks | u32 last_chunk_len | u8 fp_len | fp bytes |
     payload (each chunk's 32-bit LE words, chunk order) |
     "IDX2" | first_bytes[n] | uvarint(stream_bytes)[n] | u32 CRC-32
+The Python BoaFile writer (boa.py:107-131, :226-311) writes the same layout
+with flags 0 and a 16-byte fingerprint, blake2s(model class name).
 The CRC-32 (reflected, polynomial 0xEDB88320, boa.cpp:85-107) covers
 "IDX2"...end of the lengths.  The reader also accepts "IDX1" (uvarint
 delta-offsets then lengths, boa.cpp:240-250).
@@ -39,12 +41,16 @@ def read_uvarint(buf: bytes, pos: int):  # boa.cpp:167-176
         shift += 7
 
 
-def build(total_size, chunk_len, first_bytes, streams, warm_start=False, interleave_batch=0) -> bytes:
+def build(total_size, chunk_len, first_bytes, streams, warm_start=False, interleave_batch=0,
+          fingerprint=None) -> bytes:
     n = len(streams)
     last = total_size - (n - 1) * chunk_len if n > 1 else total_size
     flags = 1 if warm_start else 0
     head = b"BOA2" + struct.pack("<IIQIII", 1, flags, total_size, chunk_len, n, last)
-    head += bytes([4]) + struct.pack("<I", interleave_batch) if warm_start else bytes([0])
+    if fingerprint is not None:  # boa.py:120-121
+        head += bytes([len(fingerprint)]) + bytes(fingerprint)
+    else:
+        head += bytes([4]) + struct.pack("<I", interleave_batch) if warm_start else bytes([0])
     payload = b"".join(bytes(s) for s in streams)
     idx = b"IDX2" + bytes(first_bytes) + b"".join(uvarint(len(bytes(s))) for s in streams)
     return head + payload + idx + struct.pack("<I", zlib.crc32(idx) & 0xFFFFFFFF)

@@ -623,6 +623,91 @@ int orc_rc_decode_cdf(const uint32_t* Q, int n, const uint32_t* words, int n_wor
   return 0;
 }
 
+// build_cdf_fast (gpu_range_coder.py:57-79): cdf[i] = (u32)(P_i * scale) + i
+// with P_i the left-to-right fp64 sum of the first i probabilities and
+// scale = (2^24 - K) / P_K; a non-positive or non-finite P_K gives the equal
+// split acc += (2^24 - K) / K + 1.
+void orc_pyrc_cdf_rows(const float* probs, int rows, int K, uint32_t* cdf) {
+  const uint32_t total = 1u << 24, free_w = total - (uint32_t)K;
+  for (int r = 0; r < rows; ++r) {
+    const float* p = probs + (size_t)r * K;
+    uint32_t* c = cdf + (size_t)r * (K + 1);
+    double norm = 0.0;
+    for (int i = 0; i < K; ++i) norm += (double)p[i];
+    if (!(norm > 0.0) || !std::isfinite(norm)) {
+      uint32_t acc = 0;
+      for (int i = 0; i < K; ++i) { c[i] = acc; acc += free_w / (uint32_t)K + 1u; }
+    } else {
+      const double scale = (double)free_w / norm;
+      double cum = 0.0;
+      for (int i = 0; i < K; ++i) { c[i] = (uint32_t)(cum * scale) + (uint32_t)i; cum += (double)p[i]; }
+    }
+    c[K] = total;
+  }
+}
+
+namespace {
+// encode_kernel's update (gpu_range_coder.py:81-140): no clamp of prob.
+bool pyrc_symbol(Enc& st, uint32_t left, uint32_t prob, uint32_t* out, int cap) {
+  const uint64_t scale = st.range >> 24;
+  const uint64_t old_lower = st.lower;
+  st.range = scale * (uint64_t)prob;
+  st.lower = st.lower + scale * (uint64_t)left;
+  if (st.inv > 0 && st.lower + st.range > st.lower) {
+    const bool carry = st.lower < old_lower;
+    if (st.w + st.inv > cap) return false;
+    out[st.w++] = carry ? st.first_inv + 1u : st.first_inv;
+    for (int k = 1; k < st.inv; ++k) out[st.w++] = carry ? 0u : 0xFFFFFFFFu;
+    st.inv = 0;
+  }
+  while (st.range < (1ull << 32)) {
+    const uint32_t lw = (uint32_t)(st.lower >> 32);
+    st.lower <<= 32; st.range <<= 32;
+    if (st.inv > 0) { if (st.inv < 0x7FFFFFFF) st.inv++; }
+    else if (st.lower + st.range > st.lower) { if (st.w >= cap) return false; out[st.w++] = lw; }
+    else { st.inv = 1; st.first_inv = lw; }
+  }
+  return true;
+}
+}  // namespace
+
+int orc_pyrc_encode(const float* probs, const int32_t* syms, int n, int K, uint32_t* out, int cap) {
+  Enc st;
+  std::vector<uint32_t> c((size_t)K + 1);
+  for (int t = 0; t < n; ++t) {
+    const int s = syms[t];
+    if (s < 0 || s >= K) continue;
+    orc_pyrc_cdf_rows(probs + (size_t)t * K, 1, K, c.data());
+    if (!pyrc_symbol(st, c[s], c[s + 1] - c[s], out, cap)) return -1;
+  }
+  return enc_finish(st, out, cap);  // finalize_kernel (:142-168) is ker_rc_finish's rule
+}
+
+int orc_pyrc_decode(const float* probs, int n, int K, const uint32_t* words, int n_words, int32_t* syms) {
+  Dec d;
+  d.init(words, n_words);
+  std::vector<uint32_t> c((size_t)K + 1);
+  for (int t = 0; t < n; ++t) {
+    orc_pyrc_cdf_rows(probs + (size_t)t * K, 1, K, c.data());
+    const uint32_t target = d.target();
+    int i = 1;  // decode_step_kernel (:182-215): first i >= 1 with cdf[i] > target
+    while (i <= K && !(c[i] > target)) ++i;
+    int s = i - 1;
+    if (s < 0) s = 0;
+    if (s >= K) s = K - 1;
+    syms[t] = s;
+    const uint64_t scale = d.range >> 24;
+    d.lower = d.lower + scale * (uint64_t)c[s];
+    d.range = scale * (uint64_t)(c[s + 1] - c[s]);
+    while (d.range < (1ull << 32)) {
+      d.lower <<= 32; d.range <<= 32;
+      const uint32_t w = d.r < d.n ? d.in[d.r++] : 0u;
+      d.point = (d.point << 32) | w;
+    }
+  }
+  return 0;
+}
+
 int orc_compress(void* mp, const uint8_t* data, size_t n, uint32_t chunk_len, float inv_t,
                  int n_threads, uint8_t* first_bytes, uint32_t* stream_words, uint32_t pitch,
                  uint32_t* sizes) {

@@ -46,6 +46,16 @@ void orc_cdf_rows(const float* logits, int rows, float inv_temperature, uint32_t
 int orc_rc_encode_cdf(const uint32_t* Q, const uint8_t* syms, int n, uint32_t* out, int cap);
 int orc_rc_decode_cdf(const uint32_t* Q, int n, const uint32_t* words, int n_words, uint8_t* syms);
 
+/* The Python codec's coder (gpu_range_coder.py): fp32 probability rows are
+ * quantised by build_cdf_fast (gpu_range_coder.py:57-79) into K+1 integer
+ * CDF entries, then range-coded by encode_kernel / finalize_kernel /
+ * decode_step_kernel (:81-215).  probs [n][K], one stream; symbols outside
+ * [0, K) are skipped by the encoder, as in the reference.  encode returns the
+ * number of words (<= cap) or -1. */
+void orc_pyrc_cdf_rows(const float* probs, int rows, int K, uint32_t* cdf);
+int orc_pyrc_encode(const float* probs, const int32_t* syms, int n, int K, uint32_t* out, int cap);
+int orc_pyrc_decode(const float* probs, int n, int K, const uint32_t* words, int n_words, int32_t* syms);
+
 /* Chunk-parallel codec on host threads.  Chunk i covers
  * data[i*chunk_len, min(n, (i+1)*chunk_len)).  Streams are written at
  * stream_words + i*pitch_words; sizes_words[i] = words used.

@@ -4,6 +4,9 @@
 #   boa_constrictor  the reference CLI, portability_solved_cpp/README.md:11
 #                    build line plus an sm_100a target
 #   ref_logits       oracle/ref_harness.cu linked against the reference kernels
+#   _gpu_range_cuda_ext*.so  the Python codec's batch range coder: importing
+#                    gpu_range_coder.py compiles it (gpu_range_coder.py:14-367);
+#                    TMPDIR points its build folder into _ref
 # Needs the reference checkout (default /root/reference, or $BOA_REF_DIR);
 # without it the script does nothing and says so.  Outputs are git-ignored.
 set -euo pipefail
@@ -21,5 +24,12 @@ if [ ! -x "$OUT/boa_constrictor" ] || [ "${FORCE:-0}" = 1 ]; then
 fi
 if [ ! -x "$OUT/ref_logits" ] || [ "$HERE/ref_harness.cu" -nt "$OUT/ref_logits" ] || [ "${FORCE:-0}" = 1 ]; then
   nvcc -o "$OUT/ref_logits" "$HERE/ref_harness.cu" "${KERNELS[@]}" -I"$REF" "${FLAGS[@]}"
+fi
+if ! ls "$OUT"/_gpu_range_cuda_ext*.so >/dev/null 2>&1 || [ "${FORCE:-0}" = 1 ]; then
+  mkdir -p "$OUT/pyrc_build"
+  TMPDIR="$OUT/pyrc_build" python3 -c "import sys; sys.path.insert(0, sys.argv[1]); import gpu_range_coder" \
+    "$(dirname "$REF")"
+  cp "$OUT"/pyrc_build/gpu_range_build/_gpu_range_cuda_ext*.so "$OUT"/
+  rm -rf "$OUT/pyrc_build"
 fi
 echo "reference build in $OUT"

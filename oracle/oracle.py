@@ -18,6 +18,7 @@ LIB_PATH = os.path.join(HERE, "liboracle.so")
 _u8p = C.POINTER(C.c_uint8)
 _u32p = C.POINTER(C.c_uint32)
 _f32p = C.POINTER(C.c_float)
+_i32p = C.POINTER(C.c_int32)
 _lib = None
 
 
@@ -49,6 +50,9 @@ def lib():
                                         _u8p, _u32p, C.c_uint32, _u32p]
         L.orc_decompress_warm.argtypes = [C.c_void_p, _u32p, C.c_uint32, _u32p, _u8p, C.c_size_t, C.c_uint32,
                                           C.c_uint32, C.c_float, C.c_int, _u8p]
+        L.orc_pyrc_cdf_rows.argtypes = [_f32p, C.c_int, C.c_int, _u32p]
+        L.orc_pyrc_encode.argtypes = [_f32p, _i32p, C.c_int, C.c_int, _u32p, C.c_int]
+        L.orc_pyrc_decode.argtypes = [_f32p, C.c_int, C.c_int, _u32p, C.c_int, _i32p]
         _lib = L
     return _lib
 
@@ -152,3 +156,36 @@ def rc_decode_cdf(Q: np.ndarray, words: np.ndarray, n: int) -> np.ndarray:
     syms = np.zeros(max(n, 1), np.uint8)
     lib().orc_rc_decode_cdf(_p(Q, _u32p), n, _p(wbuf, _u32p), words.size, _p(syms, _u8p))
     return syms[:n]
+
+
+# ---- the Python codec's coder (gpu_range_coder.py) -------------------------
+def pyrc_cdf_rows(probs: np.ndarray) -> np.ndarray:
+    p = np.ascontiguousarray(probs, dtype=np.float32)
+    K = p.shape[-1]
+    p = p.reshape(-1, K)
+    out = np.empty((p.shape[0], K + 1), np.uint32)
+    lib().orc_pyrc_cdf_rows(_p(p, _f32p), p.shape[0], K, _p(out, _u32p))
+    return out
+
+
+def pyrc_encode(probs: np.ndarray, syms: np.ndarray) -> np.ndarray:
+    """One stream: probs [n][K] float32, syms [n] int32 -> uint32 words."""
+    p = np.ascontiguousarray(probs, dtype=np.float32)
+    s = np.ascontiguousarray(syms, dtype=np.int32)
+    n, K = p.shape
+    cap = 3 * n + 16
+    out = np.zeros(cap, np.uint32)
+    w = lib().orc_pyrc_encode(_p(p, _f32p), _p(s, _i32p), n, K, _p(out, _u32p), cap)
+    if w < 0:
+        raise RuntimeError("stream overflow")
+    return out[:w].copy()
+
+
+def pyrc_decode(probs: np.ndarray, words: np.ndarray) -> np.ndarray:
+    p = np.ascontiguousarray(probs, dtype=np.float32)
+    n, K = p.shape
+    wd = np.ascontiguousarray(words, dtype=np.uint32)
+    wbuf = wd if wd.size else np.zeros(1, np.uint32)
+    out = np.zeros(max(n, 1), np.int32)
+    lib().orc_pyrc_decode(_p(p, _f32p), n, K, _p(wbuf, _u32p), wd.size, _p(out, _i32p))
+    return out[:n]

@@ -14,6 +14,9 @@ manifest.json, so only reference OUTPUTS are stored):
                          pins quantiser + range coder + BOA2 container bit-exact
   ref_exact_warm.boa     the same with --warm-start --gpu-batch 3: pins the
                          warm-start container fields (flags bit0, batch)
+  ref_pyrc.npz           streams of the Python codec's batch coder
+                         (gpu_range_coder.py RangeCoderBatch, built by
+                         oracle/build_ref.sh) over seeded probability rows
   ref_rand_d256L8.boa    reference CLI compress of 64 KiB of particle records
                          under the configs[0] model: container layout and the
                          reference's bits/byte
@@ -48,6 +51,59 @@ LOGIT_CFGS = [dict(name="d64L2", d_model=64, n_layers=2, seed=3, B=3, T=40, tok_
               dict(name="gru_d64L2", backbone="gru", std=0.1, d_model=64, n_layers=2, seed=3, B=3, T=40,
                    tok_seed=5)]
 RAND = dict(d_model=256, n_layers=8, seed=0, n_bytes=65536, data_seed=1, chunk=4096, batch=16)
+# Python-codec coder cases: N streams x T steps over K symbols
+PYRC = [dict(name="k256", seed=21, N=48, T=160, K=256, alpha=0.1),
+        dict(name="k7", seed=22, N=33, T=90, K=7, alpha=0.5),
+        dict(name="k1000", seed=23, N=9, T=40, K=1000, alpha=0.05)]
+
+
+def pyrc_inputs(cfg):
+    """probs [T][N][K] float32 (Dirichlet rows with some exact zeros and a few
+    all-zero rows, which take the equal-split branch), symbols [T][N] int32
+    drawn from each row, and a ragged activity mask [T][N] (stream n is active
+    for t < len_n), as codec.compress_GPU masks finished chunks."""
+    rng = np.random.default_rng(cfg["seed"])
+    T, N, K = cfg["T"], cfg["N"], cfg["K"]
+    probs = rng.dirichlet(np.full(K, cfg["alpha"]), size=(T, N)).astype(np.float32)
+    probs[rng.random((T, N, K)) < 0.02] = 0.0
+    probs[rng.random((T, N)) < 0.01] = 0.0
+    syms = np.empty((T, N), np.int32)
+    u = rng.random((T, N))
+    for t in range(T):
+        for n in range(N):
+            p = probs[t, n].astype(np.float64)
+            c = np.cumsum(p / p.sum()) if p.sum() > 0 else np.arange(1, K + 1) / K
+            syms[t, n] = min(int(np.searchsorted(c, u[t, n], side="right")), K - 1)
+    lens = rng.integers(1, T + 1, N)
+    lens[0] = T
+    mask = np.arange(T)[:, None] < lens[None, :]
+    return probs, syms, mask
+
+
+def run_ref_pyrc(ext, cfg):
+    """Encode then decode one case through the reference extension."""
+    import torch
+    probs, syms, mask = pyrc_inputs(cfg)
+    T, N, K = cfg["T"], cfg["N"], cfg["K"]
+    pitch = (max(256, T * 8) + 3) // 4  # the gpu.queue.RangeCoderBatch default
+    P = torch.from_numpy(probs).cuda()
+    S = torch.from_numpy(syms).cuda()
+    Mk = torch.from_numpy(mask.astype(np.uint8)).cuda()
+    enc = ext.RangeCoderBatch(N, K, pitch)
+    for t in range(T):
+        enc.encode_step_from_device(S[t].data_ptr(), P[t].data_ptr(), Mk[t].data_ptr())
+    enc.finalize()
+    streams = [np.asarray(a, np.uint32) for a in enc.get_compressed_host()]
+    dec = ext.RangeCoderBatch(N, K, pitch)
+    dec.load_compressed_from_host(streams)
+    dec.init_decoder_from_current_bytes()
+    out = torch.zeros(N, dtype=torch.int32, device="cuda")
+    got = np.zeros((T, N), np.int32)
+    for t in range(T):
+        dec.decode_step_to_device(P[t].data_ptr(), out.data_ptr(), Mk[t].data_ptr())
+        got[t] = out.cpu().numpy()
+    decoded_ok = bool(np.array_equal(np.where(mask, got, 0), np.where(mask, syms, 0)))
+    return streams, decoded_ok, hashlib.sha256(probs.tobytes()).hexdigest()
 
 
 def exact_input(cfg):
@@ -141,6 +197,22 @@ def main(out_dir):
     run([os.path.join(REF, "boa_constrictor"), "decompress", w, boa_rw, back_rw, str(RAND["d_model"]),
          str(RAND["n_layers"])])
     man["rand_warm_result"] = dict(ref_roundtrip=open(back_rw, "rb").read() == data)
+    # the Python codec's batch coder, built from gpu_range_coder.py
+    import glob
+    import importlib.machinery
+    so = glob.glob(os.path.join(REF, "_gpu_range_cuda_ext*.so"))[0]
+    loader = importlib.machinery.ExtensionFileLoader("_gpu_range_cuda_ext", so)
+    ext = importlib.util.module_from_spec(importlib.util.spec_from_loader("_gpu_range_cuda_ext", loader))
+    loader.exec_module(ext)
+    man["pyrc"] = PYRC
+    man["pyrc_result"] = {}
+    arrays = {}
+    for c in PYRC:
+        streams, ok, probs_sha = run_ref_pyrc(ext, c)
+        arrays[c["name"] + "_sizes"] = np.array([len(x) for x in streams], np.int32)
+        arrays[c["name"] + "_words"] = np.concatenate(streams).astype(np.uint32)
+        man["pyrc_result"][c["name"]] = dict(ref_decoded=ok, probs_sha=probs_sha)
+    np.savez_compressed(os.path.join(out_dir, "ref_pyrc.npz"), **arrays)
     for f in os.listdir(tmp):
         os.remove(os.path.join(tmp, f))
     os.rmdir(tmp)

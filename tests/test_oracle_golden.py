@@ -118,3 +118,48 @@ def test_oracle_rnn_roundtrip(oracle, boa, weights, backbone):
     assert m.decompress(fb, st, len(data), 300) == data
     tok = np.frombuffer(data[:64], np.uint8).reshape(2, 32)
     assert np.array_equal(m.logits(tok, 0), m.logits(tok, 1))
+
+
+@pytest.mark.parametrize("case", ["k256", "k7", "k1000"])
+def test_oracle_pyrc_matches_reference_streams(oracle, manifest, golden_mod, case):
+    """The Python codec's coder (gpu_range_coder.py): the oracle's restatement
+    of build_cdf_fast + the range coder reproduces the reference extension's
+    streams word for word, and the reference decoded its own streams."""
+    c = next(x for x in manifest["pyrc"] if x["name"] == case)
+    res = manifest["pyrc_result"][case]
+    assert res["ref_decoded"]
+    probs, syms, mask = golden_mod.pyrc_inputs(c)
+    import hashlib
+    assert hashlib.sha256(probs.tobytes()).hexdigest() == res["probs_sha"]
+    z = np.load(f"{GOLDEN}/ref_pyrc.npz")
+    sizes, words = z[case + "_sizes"], z[case + "_words"]
+    o = 0
+    for n in range(c["N"]):
+        act = mask[:, n]
+        w = oracle.pyrc_encode(probs[act, n], syms[act, n])
+        assert np.array_equal(w, words[o:o + sizes[n]]), n
+        assert np.array_equal(oracle.pyrc_decode(probs[act, n], w), syms[act, n])
+        o += int(sizes[n])
+    assert o == words.size
+
+
+def test_python_dialect_container(boa, boa2):
+    """A container in the Python BoaFile dialect (16-byte blake2s fingerprint,
+    flags 0) is written byte-identically to the restatement and parsed back."""
+    import hashlib
+    fp = hashlib.blake2s(b"BoaBytePredictor", digest_size=16).digest()
+    assert boa.python_fingerprint() == fp
+    rng = np.random.default_rng(9)
+    sizes = [5, 0, 17, 3]
+    words = rng.integers(0, 2**32, sum(sizes), dtype=np.uint64).astype(np.uint32)
+    fb = [1, 2, 3, 4]
+    streams, o = [], 0
+    for s in sizes:
+        streams.append(words[o:o + s].tobytes())
+        o += s
+    total = 3 * 100 + 41
+    ours = boa.boa2_build(total, 100, fb, sizes, words, fingerprint=fp)
+    assert ours == boa2.build(total, 100, fb, streams, fingerprint=fp)
+    info = boa.boa2_parse(ours)
+    assert info["fingerprint"] == fp and info["flags"] == 0 and info["interleave_batch"] == 0
+    assert [bytes(s) for s in info["streams"]] == streams
