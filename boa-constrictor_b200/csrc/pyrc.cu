@@ -9,11 +9,12 @@
 // path can be written or read with this coder in place of the reference's.
 //
 // The reference runs one thread per stream, builds all K+1 CDF entries in a
-// 1025-entry local array and reads its row with strided scalar loads.  Here
-// one warp handles a stream: the row is read coalesced, the left-to-right fp64
-// prefix sums (whose rounding fixes the CDF) run lane to lane through
-// shuffles, every lane converts its own entries, and the decoder's symbol
-// search is one ballot.  Lane 0 alone updates the coder state.
+// 1025-entry local array and reads its row with strided scalar loads.  Here a
+// warp stages the rows of 32 streams through shared memory with coalesced
+// loads and each lane runs its own row's fp64 prefix sum (whose rounding fixes
+// the CDF).  The encoder needs only P_s, P_s+1 and P_K, so it reads the row
+// once and builds no table; the decoder records P at every 64-entry slab
+// start, picks the one slab holding its target and re-reads only that slab.
 #include <string>
 
 #include "kernels.cuh"
@@ -33,92 +34,58 @@ struct PyDec {
 constexpr unsigned kFull = 0xffffffffu;
 constexpr uint32_t kPyTotal = 1u << 24;
 
-// The row quantiser, lane-distributed: lane l owns entries [l*E, l*E + E).
-template <int E>
-struct PyRow {
-  double cum[E];  // P_i, the fp64 sum of probabilities 0..i-1 (left to right)
-  double scale;   // (2^24 - K) / P_K
-  uint32_t step;  // equal-split increment when P_K is not positive and finite
-  bool equal;
-  int base, K;
+// A warp codes 32 streams, one per lane.  Rows are staged through shared
+// memory in slabs of 64 columns (coalesced 128-byte row segments; the tile's
+// row stride of 65 words keeps both the staging stores and each lane's reads
+// of its own row free of bank conflicts).  Each lane then runs the fp64
+// left-to-right sum of its own row -- the order build_cdf_fast rounds in --
+// so the chain costs one add per element instead of occupying the warp.
+constexpr int kSlab = 64;
+constexpr int kPyWarps = 8;
+constexpr int kMaxSlabs = 1024 / kSlab + 1;
 
-  __device__ __forceinline__ void build(const float* __restrict__ row, int K_, int lane) {
-    K = K_;
-    base = lane * E;
-    float p[E];
-    if (E >= 4 && (K & 3) == 0) {
-#pragma unroll
-      for (int v = 0; v < E / 4; ++v) {
-        const int i = base + 4 * v;
-        float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < K) q = __ldg(reinterpret_cast<const float4*>(row + i));
-        p[4 * v] = q.x; p[4 * v + 1] = q.y; p[4 * v + 2] = q.z; p[4 * v + 3] = q.w;
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < E; ++e) p[e] = base + e < K ? __ldg(row + base + e) : 0.f;
-    }
-    // sequential chain: lane l starts from the sum lane l-1 ended with
-    double carry = 0.0, c = 0.0;
-    for (int src = 0; src < 32; ++src) {
-      if (lane == src) {
-        c = carry;
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          cum[e] = c;
-          if (base + e < K) c = __dadd_rn(c, (double)p[e]);
-        }
-      }
-      carry = __shfl_sync(kFull, c, src);
-    }
-    const double norm = carry;
-    const uint32_t free_w = kPyTotal - (uint32_t)K;
-    equal = !(norm > 0.0) || !isfinite(norm);
-    scale = equal ? 0.0 : __ddiv_rn((double)free_w, norm);
-    step = free_w / (uint32_t)K + 1u;
-  }
-  // cdf of entry base + e (e < E, base + e < K)
-  __device__ __forceinline__ uint32_t at(int e) const {
-    const uint32_t i = (uint32_t)(base + e);
-    return equal ? i * step : __double2uint_rz(__dmul_rn(cum[e], scale)) + i;
-  }
-  // cdf[i] for any 0 <= i <= K, gathered from its owner lane (all lanes call)
-  __device__ __forceinline__ uint32_t get(int i) const {
-    uint32_t mine = 0;
-#pragma unroll
-    for (int e = 0; e < E; ++e)
-      if (base + e == i) mine = at(e);
-    const uint32_t v = __shfl_sync(kFull, mine, (i < K ? i : 0) / E);
-    return i >= K ? kPyTotal : v;
-  }
+struct PyTile {
+  float t[32 * (kSlab + 1)];
+  double bcum[32 * kMaxSlabs];  // decode: P at every slab start, per lane
 };
+
+// columns [c0, c0 + 64) of rows row0 .. row0 + 31 (rows >= N read as zero)
+__device__ __forceinline__ void py_stage(const float* __restrict__ probs, long long row0, int N, int K, int c0,
+                                         float* __restrict__ t, int lane) {
+  __syncwarp();
+#pragma unroll 16
+  for (int r = 0; r < 32; ++r) {
+    const long long row = row0 + r;
+    float a = 0.f, b = 0.f;
+    if (row < N) {
+      const float* src = probs + row * K + c0;
+      if (c0 + lane < K) a = __ldg(src + lane);
+      if (c0 + 32 + lane < K) b = __ldg(src + 32 + lane);
+    }
+    t[r * (kSlab + 1) + lane] = a;
+    t[r * (kSlab + 1) + 32 + lane] = b;
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ uint32_t py_cdf(double cum, double scale, uint32_t i) {
+  return __double2uint_rz(__dmul_rn(cum, scale)) + i;
+}
 
 __device__ __forceinline__ void py_put(uint32_t* out, int pitch, int& w, uint32_t v) {
   if (w < pitch) out[w] = v;
   ++w;  // counted past the pitch: finalize reports the overflow
 }
 
-template <int E>
-__global__ void __launch_bounds__(128) pyrc_encode_kernel(const int32_t* __restrict__ syms,
-                                                          const float* __restrict__ probs, int N, int K,
-                                                          uint32_t* __restrict__ words, PyEnc* __restrict__ states,
-                                                          int pitch, const uint8_t* __restrict__ mask) {
-  const int idx = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
-  const int lane = threadIdx.x & 31;
-  if (idx >= N) return;
-  if (mask && mask[idx] == 0) return;
-  const int s = syms[idx];
-  if (s < 0 || s >= K) return;
-  PyRow<E> row;
-  row.build(probs + (size_t)idx * K, K, lane);
-  const uint32_t left = row.get(s), right = row.get(s + 1);
-  if (lane != 0) return;
+// encode_kernel's state update for the interval [left, right) (gpu_range_coder.py:96-140)
+__device__ __forceinline__ void py_encode_update(PyEnc* __restrict__ states, uint32_t* __restrict__ words, int pitch,
+                                                 long long idx, uint32_t left, uint32_t right) {
   PyEnc st = states[idx];
   uint32_t* out = words + (size_t)idx * pitch;
-  const unsigned long long scale = st.range >> 24;
+  const unsigned long long scl = st.range >> 24;
   const unsigned long long old_lower = st.lower;
-  st.range = scale * (unsigned long long)(right - left);
-  st.lower = st.lower + scale * (unsigned long long)left;
+  st.range = scl * (unsigned long long)(right - left);
+  st.lower = st.lower + scl * (unsigned long long)left;
   if (st.inv > 0 && st.lower + st.range > st.lower) {
     const bool carry = st.lower < old_lower;
     py_put(out, pitch, st.w, carry ? st.first_inv + 1u : st.first_inv);
@@ -141,41 +108,50 @@ __global__ void __launch_bounds__(128) pyrc_encode_kernel(const int32_t* __restr
   states[idx] = st;
 }
 
-template <int E>
-__global__ void __launch_bounds__(128) pyrc_decode_kernel(const float* __restrict__ probs, int N, int K,
-                                                          const uint32_t* __restrict__ words,
-                                                          const int32_t* __restrict__ sizes,
-                                                          PyDec* __restrict__ states, int pitch,
-                                                          int32_t* __restrict__ out_syms,
-                                                          const uint8_t* __restrict__ mask) {
-  const int idx = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
-  const int lane = threadIdx.x & 31;
-  if (idx >= N) return;
-  if (mask && mask[idx] == 0) return;
-  PyRow<E> row;
-  row.build(probs + (size_t)idx * K, K, lane);
-  PyDec st = states[idx];  // every lane reads the same 32 bytes
-  const unsigned long long scale = st.range >> 24;
-  unsigned long long q = (st.point - st.lower) / scale;
-  if (q >= (1ull << 24)) q = (1ull << 24) - 1ull;
-  const uint32_t target = (uint32_t)q;
-  // first i >= 1 with cdf[i] > target (cdf[K] = 2^24 always qualifies)
-  int first = K;
-#pragma unroll
-  for (int e = E - 1; e >= 0; --e) {
-    const int i = row.base + e;
-    if (i >= 1 && i < K && row.at(e) > target) first = i;
+// decode_step_kernel's search (gpu_range_coder.py:196-201): the first i >= 1
+// with cdf[i] > target (cdf[K] = 2^24 always qualifies); [left, right) =
+// [cdf[i-1], cdf[i]).  `row` holds the K probabilities, bcum the sum P at
+// every 64-entry slab start and `norm` = P_K.  Entries strictly increase when
+// no probability is negative, so the scan starts at the last slab whose
+// first entry is <= target; otherwise it walks every entry from 1 as the
+// reference does.
+__device__ __forceinline__ int py_search(const float* row, const double* bcum, int K, double norm, bool neg,
+                                         uint32_t target, uint32_t& left, uint32_t& right) {
+  const uint32_t free_w = kPyTotal - (uint32_t)K;
+  if (!(norm > 0.0) || !isfinite(norm)) {
+    const uint32_t step = free_w / (uint32_t)K + 1u;
+    const int i = (int)min((uint32_t)K, target / step + 1u);
+    left = (uint32_t)(i - 1) * step;
+    right = i == K ? kPyTotal : (uint32_t)i * step;
+    return i;
   }
-  const unsigned hit = __ballot_sync(kFull, first < K);
-  const int i = hit ? __shfl_sync(kFull, first, __ffs(hit) - 1) : K;
-  int s = i - 1;
-  if (s < 0) s = 0;
-  if (s >= K) s = K - 1;
-  const uint32_t left = row.get(s), right = row.get(s + 1);
-  if (lane != 0) return;
-  out_syms[idx] = s;
-  st.lower = st.lower + scale * (unsigned long long)left;
-  st.range = scale * (unsigned long long)(right - left);
+  const double scale = __ddiv_rn((double)free_w, norm);
+  const int nslab = (K + kSlab - 1) / kSlab;
+  int k = 0;
+  if (!neg)
+    for (int kk = 1; kk < nslab; ++kk)
+      if (py_cdf(bcum[kk], scale, (uint32_t)(kk * kSlab)) <= target) k = kk;
+  double cc = bcum[k];  // bcum[0] = 0
+  uint32_t prev = py_cdf(cc, scale, (uint32_t)(k * kSlab));
+  for (int j = k * kSlab; j < K; ++j) {
+    cc = __dadd_rn(cc, (double)row[j]);
+    const int ii = j + 1;
+    const uint32_t v = ii == K ? kPyTotal : py_cdf(cc, scale, (uint32_t)ii);
+    if (v > target) { left = prev; right = v; return ii; }
+    prev = v;
+  }
+  left = prev;  // not reached: cdf[K] > target
+  right = kPyTotal;
+  return K;
+}
+
+// decode_step_kernel's update and refill (gpu_range_coder.py:202-214)
+__device__ __forceinline__ void py_decode_update(PyDec& st, const uint32_t* __restrict__ words,
+                                                 const int32_t* __restrict__ sizes, int pitch, long long idx,
+                                                 uint32_t left, uint32_t right) {
+  const unsigned long long scl = st.range >> 24;
+  st.lower = st.lower + scl * (unsigned long long)left;
+  st.range = scl * (unsigned long long)(right - left);
   const uint32_t* in = words + (size_t)idx * pitch;
   const int n = sizes[idx];
   while (st.range < (1ull << 32)) {
@@ -184,6 +160,207 @@ __global__ void __launch_bounds__(128) pyrc_decode_kernel(const float* __restric
     const uint32_t w = st.r < n ? in[st.r++] : 0u;
     st.point = (st.point << 32) | (unsigned long long)w;
   }
+}
+
+__global__ void __launch_bounds__(32 * kPyWarps) pyrc_encode_kernel(const int32_t* __restrict__ syms,
+                                                                    const float* __restrict__ probs, int N, int K,
+                                                                    uint32_t* __restrict__ words,
+                                                                    PyEnc* __restrict__ states, int pitch,
+                                                                    const uint8_t* __restrict__ mask) {
+  extern __shared__ __align__(16) unsigned char py_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* t = reinterpret_cast<float*>(py_smem) + warp * 32 * (kSlab + 1);
+  const long long row0 = ((long long)blockIdx.x * kPyWarps + warp) * 32;
+  if (row0 >= N) return;
+  const long long idx = row0 + lane;
+  int s = -1;
+  if (idx < N && (!mask || mask[idx] != 0)) s = syms[idx];
+  const bool active = s >= 0 && s < K;
+  if (!__any_sync(0xffffffffu, active)) return;
+  double c = 0.0, cum_s = 0.0, cum_s1 = 0.0;
+  for (int c0 = 0; c0 < K; c0 += kSlab) {
+    py_stage(probs, row0, N, K, c0, t, lane);
+    const int n = min(kSlab, K - c0);
+    const float* mine = t + lane * (kSlab + 1);
+    for (int j = 0; j < n; ++j) {
+      if (c0 + j == s) cum_s = c;
+      c = __dadd_rn(c, (double)mine[j]);
+      if (c0 + j == s) cum_s1 = c;
+    }
+  }
+  if (!active) return;
+  const uint32_t free_w = kPyTotal - (uint32_t)K;
+  uint32_t left, right;
+  if (!(c > 0.0) || !isfinite(c)) {
+    const uint32_t step = free_w / (uint32_t)K + 1u;
+    left = (uint32_t)s * step;
+    right = s + 1 == K ? kPyTotal : (uint32_t)(s + 1) * step;
+  } else {
+    const double scale = __ddiv_rn((double)free_w, c);
+    left = py_cdf(cum_s, scale, (uint32_t)s);
+    right = s + 1 == K ? kPyTotal : py_cdf(cum_s1, scale, (uint32_t)(s + 1));
+  }
+  py_encode_update(states, words, pitch, idx, left, right);
+}
+
+__global__ void __launch_bounds__(32 * kPyWarps) pyrc_decode_kernel(const float* __restrict__ probs, int N, int K,
+                                                                    const uint32_t* __restrict__ words,
+                                                                    const int32_t* __restrict__ sizes,
+                                                                    PyDec* __restrict__ states, int pitch,
+                                                                    int32_t* __restrict__ out_syms,
+                                                                    const uint8_t* __restrict__ mask) {
+  extern __shared__ __align__(16) unsigned char py_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  PyTile* tile = reinterpret_cast<PyTile*>(py_smem) + warp;
+  float* t = tile->t;
+  double* bcum = tile->bcum + lane * kMaxSlabs;
+  const long long row0 = ((long long)blockIdx.x * kPyWarps + warp) * 32;
+  if (row0 >= N) return;
+  const long long idx = row0 + lane;
+  const bool active = idx < N && (!mask || mask[idx] != 0);
+  if (!__any_sync(0xffffffffu, active)) return;
+  // pass 1: P_K, with P recorded at every slab start; any negative entry
+  // (not a softmax row) sends the search through every entry in order
+  double c = 0.0;
+  bool neg = false;
+  for (int c0 = 0, k = 0; c0 < K; c0 += kSlab, ++k) {
+    py_stage(probs, row0, N, K, c0, t, lane);
+    bcum[k] = c;
+    const int n = min(kSlab, K - c0);
+    const float* mine = t + lane * (kSlab + 1);
+    for (int j = 0; j < n; ++j) {
+      neg |= mine[j] < 0.f;
+      c = __dadd_rn(c, (double)mine[j]);
+    }
+  }
+  if (!active) return;
+  PyDec st = states[idx];
+  const unsigned long long scl = st.range >> 24;
+  unsigned long long q = (st.point - st.lower) / scl;
+  if (q >= (1ull << 24)) q = (1ull << 24) - 1ull;
+  const uint32_t target = (uint32_t)q;
+  uint32_t left, right;
+  const int i = py_search(probs + idx * K, bcum, K, c, neg, target, left, right);
+  out_syms[idx] = i - 1;
+  py_decode_update(st, words, sizes, pitch, idx, left, right);
+  states[idx] = st;
+}
+
+// ---- rows of K <= 256 (K % 4 == 0): whole tile by bulk async copy ----------
+// The slab loop above keeps only 2 KB per warp in flight and stages serially.
+// For the Python codec's K = 256 the warp's 32 rows (32 KB) fit in shared
+// memory, so each lane issues one bulk copy for its row onto a single
+// mbarrier and the whole tile is in flight at once.  Rows sit 1040 B apart:
+// 16-byte aligned for the copies, and the 128-bit reads of 8 consecutive
+// lanes (one shared-memory phase) land on distinct bank groups.
+constexpr int kBulkStride = 260;
+constexpr int kBulkWarps = 2;
+constexpr int kBulkMaxK = 256;
+
+struct PyBulkTile {
+  float t[32 * kBulkStride];
+  double bcum[32 * (kBulkMaxK / kSlab)];  // decode: P at every 64-entry slab start
+  uint64_t bar;
+  uint64_t pad;
+};
+
+// false when the copies did not land within the wait limit (error word set)
+__device__ __forceinline__ bool py_stage_bulk(const float* __restrict__ probs, long long row0, int N, int K,
+                                              PyBulkTile* tl, int lane) {
+  const int rows = (int)min(32LL, (long long)N - row0);
+  if (lane == 0) {
+    mbar_init(&tl->bar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&tl->bar, (uint32_t)(rows * K * 4));
+  }
+  __syncwarp();
+  if (lane < rows) bulk_load(tl->t + lane * kBulkStride, probs + (row0 + lane) * K, (uint32_t)K * 4u, &tl->bar);
+  return mbar_wait(&tl->bar, 0);
+}
+
+__global__ void __launch_bounds__(32 * kBulkWarps) pyrc_encode_bulk_kernel(const int32_t* __restrict__ syms,
+                                                                           const float* __restrict__ probs, int N,
+                                                                           int K, uint32_t* __restrict__ words,
+                                                                           PyEnc* __restrict__ states, int pitch,
+                                                                           const uint8_t* __restrict__ mask) {
+  extern __shared__ __align__(16) unsigned char py_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  PyBulkTile* tl = reinterpret_cast<PyBulkTile*>(py_smem) + warp;
+  const long long row0 = ((long long)blockIdx.x * kBulkWarps + warp) * 32;
+  if (row0 >= N) return;
+  const long long idx = row0 + lane;
+  int s = -1;
+  if (idx < N && (!mask || mask[idx] != 0)) s = syms[idx];
+  const bool active = s >= 0 && s < K;
+  if (!__any_sync(0xffffffffu, active)) return;
+  if (!py_stage_bulk(probs, row0, N, K, tl, lane)) return;
+  if (!active) return;
+  const float4* r4 = reinterpret_cast<const float4*>(tl->t + lane * kBulkStride);
+  double c = 0.0, cum_s = 0.0, cum_s1 = 0.0;
+  const int qs = s >> 2;
+  for (int q = 0; q < (K >> 2); ++q) {
+    const float4 v = r4[q];
+    const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (q == qs && u == (s & 3)) cum_s = c;
+      c = __dadd_rn(c, (double)e[u]);
+      if (q == qs && u == (s & 3)) cum_s1 = c;
+    }
+  }
+  const uint32_t free_w = kPyTotal - (uint32_t)K;
+  uint32_t left, right;
+  if (!(c > 0.0) || !isfinite(c)) {
+    const uint32_t step = free_w / (uint32_t)K + 1u;
+    left = (uint32_t)s * step;
+    right = s + 1 == K ? kPyTotal : (uint32_t)(s + 1) * step;
+  } else {
+    const double scale = __ddiv_rn((double)free_w, c);
+    left = py_cdf(cum_s, scale, (uint32_t)s);
+    right = s + 1 == K ? kPyTotal : py_cdf(cum_s1, scale, (uint32_t)(s + 1));
+  }
+  py_encode_update(states, words, pitch, idx, left, right);
+}
+
+__global__ void __launch_bounds__(32 * kBulkWarps) pyrc_decode_bulk_kernel(const float* __restrict__ probs, int N,
+                                                                           int K, const uint32_t* __restrict__ words,
+                                                                           const int32_t* __restrict__ sizes,
+                                                                           PyDec* __restrict__ states, int pitch,
+                                                                           int32_t* __restrict__ out_syms,
+                                                                           const uint8_t* __restrict__ mask) {
+  extern __shared__ __align__(16) unsigned char py_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  PyBulkTile* tl = reinterpret_cast<PyBulkTile*>(py_smem) + warp;
+  const long long row0 = ((long long)blockIdx.x * kBulkWarps + warp) * 32;
+  if (row0 >= N) return;
+  const long long idx = row0 + lane;
+  const bool active = idx < N && (!mask || mask[idx] != 0);
+  if (!__any_sync(0xffffffffu, active)) return;
+  if (!py_stage_bulk(probs, row0, N, K, tl, lane)) return;
+  if (!active) return;
+  const float* row = tl->t + lane * kBulkStride;
+  const float4* r4 = reinterpret_cast<const float4*>(row);
+  double* bcum = tl->bcum + lane * (kBulkMaxK / kSlab);
+  double c = 0.0;
+  bool neg = false;
+  for (int q = 0; q < (K >> 2); ++q) {
+    if ((q & (kSlab / 4 - 1)) == 0) bcum[q / (kSlab / 4)] = c;
+    const float4 v = r4[q];
+    neg |= v.x < 0.f || v.y < 0.f || v.z < 0.f || v.w < 0.f;
+    c = __dadd_rn(c, (double)v.x);
+    c = __dadd_rn(c, (double)v.y);
+    c = __dadd_rn(c, (double)v.z);
+    c = __dadd_rn(c, (double)v.w);
+  }
+  PyDec st = states[idx];
+  const unsigned long long scl = st.range >> 24;
+  unsigned long long q = (st.point - st.lower) / scl;
+  if (q >= (1ull << 24)) q = (1ull << 24) - 1ull;
+  const uint32_t target = (uint32_t)q;
+  uint32_t left, right;
+  const int i = py_search(row, bcum, K, c, neg, target, left, right);
+  out_syms[idx] = i - 1;
+  py_decode_update(st, words, sizes, pitch, idx, left, right);
   states[idx] = st;
 }
 
@@ -228,15 +405,22 @@ __global__ void pyrc_init_dec_kernel(const uint32_t* words, const int32_t* sizes
   states[idx] = st;
 }
 
-template <int E>
-static void pyrc_launch_enc(const int32_t* syms, const float* probs, int N, int K, uint32_t* words, PyEnc* st,
-                            int pitch, const uint8_t* mask, cudaStream_t s) {
-  pyrc_encode_kernel<E><<<(unsigned)((N + 3) / 4), 128, 0, s>>>(syms, probs, N, K, words, st, pitch, mask);
-}
-template <int E>
-static void pyrc_launch_dec(const float* probs, int N, int K, const uint32_t* words, const int32_t* sizes,
-                            PyDec* st, int pitch, int32_t* out, const uint8_t* mask, cudaStream_t s) {
-  pyrc_decode_kernel<E><<<(unsigned)((N + 3) / 4), 128, 0, s>>>(probs, N, K, words, sizes, st, pitch, out, mask);
+constexpr size_t kPyEncSmem = (size_t)kPyWarps * 32 * (kSlab + 1) * sizeof(float);
+constexpr size_t kPyDecSmem = (size_t)kPyWarps * sizeof(PyTile);
+constexpr size_t kPyBulkSmem = (size_t)kBulkWarps * sizeof(PyBulkTile);
+
+static cudaError_t pyrc_prepare() {
+  static bool done = false;
+  if (done) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(pyrc_encode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPyEncSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(pyrc_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPyDecSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(pyrc_encode_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPyBulkSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(pyrc_decode_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPyBulkSmem);
+  if (e == cudaSuccess) done = true;
+  return e;
 }
 
 }  // namespace boa
@@ -262,7 +446,10 @@ int pyrc_fail(boa_pyrc* h, int code, const std::string& msg) {
 int pyrc_cuda(boa_pyrc* h, cudaError_t e, const char* where) {
   return pyrc_fail(h, BOA_E_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
 }
-int pyrc_lanes(int K) { return K <= 32 ? 1 : K <= 64 ? 2 : K <= 128 ? 4 : K <= 256 ? 8 : K <= 512 ? 16 : 32; }
+// the bulk-copy kernels need 16-byte aligned rows: K % 4 == 0 and an aligned base
+bool pyrc_bulk_ok(const boa_pyrc* h, const float* probs) {
+  return h->K <= boa::kBulkMaxK && (h->K & 3) == 0 && ((uintptr_t)probs & 15) == 0;
+}
 }  // namespace
 
 extern "C" {
@@ -276,6 +463,7 @@ int boa_pyrc_create(int n_streams, int vocab, int pitch_words, int device, boa_p
   h->device = device; h->N = n_streams; h->K = vocab; h->pitch = pitch_words;
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return pyrc_cuda(nullptr, e, "cudaSetDevice");
+  if ((e = boa::pyrc_prepare()) != cudaSuccess) return pyrc_cuda(nullptr, e, "coder kernel setup");
   auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
   const size_t N = (size_t)n_streams;
   const size_t b_enc = al(N * sizeof(boa::PyEnc)), b_dec = al(N * sizeof(boa::PyDec)),
@@ -305,13 +493,14 @@ int boa_pyrc_encode_step(boa_pyrc* h, const int32_t* d_symbols, const float* d_p
   if (!h || !d_symbols || !d_probs) return pyrc_fail(h, BOA_E_INVALID, "null argument");
   cudaSetDevice(h->device);
   cudaStream_t s = (cudaStream_t)stream;
-  switch (pyrc_lanes(h->K)) {
-    case 1: boa::pyrc_launch_enc<1>(d_symbols, d_probs, h->N, h->K, h->words, h->enc, h->pitch, d_mask, s); break;
-    case 2: boa::pyrc_launch_enc<2>(d_symbols, d_probs, h->N, h->K, h->words, h->enc, h->pitch, d_mask, s); break;
-    case 4: boa::pyrc_launch_enc<4>(d_symbols, d_probs, h->N, h->K, h->words, h->enc, h->pitch, d_mask, s); break;
-    case 8: boa::pyrc_launch_enc<8>(d_symbols, d_probs, h->N, h->K, h->words, h->enc, h->pitch, d_mask, s); break;
-    case 16: boa::pyrc_launch_enc<16>(d_symbols, d_probs, h->N, h->K, h->words, h->enc, h->pitch, d_mask, s); break;
-    default: boa::pyrc_launch_enc<32>(d_symbols, d_probs, h->N, h->K, h->words, h->enc, h->pitch, d_mask, s); break;
+  if (pyrc_bulk_ok(h, d_probs)) {
+    const unsigned grid = (unsigned)((h->N + 32 * boa::kBulkWarps - 1) / (32 * boa::kBulkWarps));
+    boa::pyrc_encode_bulk_kernel<<<grid, 32 * boa::kBulkWarps, boa::kPyBulkSmem, s>>>(
+        d_symbols, d_probs, h->N, h->K, h->words, h->enc, h->pitch, d_mask);
+  } else {
+    const unsigned grid = (unsigned)((h->N + 32 * boa::kPyWarps - 1) / (32 * boa::kPyWarps));
+    boa::pyrc_encode_kernel<<<grid, 32 * boa::kPyWarps, boa::kPyEncSmem, s>>>(d_symbols, d_probs, h->N, h->K,
+                                                                             h->words, h->enc, h->pitch, d_mask);
   }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? BOA_OK : pyrc_cuda(h, e, "encode step launch");
@@ -335,6 +524,14 @@ int boa_pyrc_read(boa_pyrc* h, uint32_t* words_host, int32_t* sizes_host, void* 
     e = cudaMemcpyAsync(words_host, h->words, (size_t)h->N * h->pitch * 4, cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return pyrc_cuda(h, e, "reading streams");
+  int code = 0;
+  if ((e = cudaMemcpyFromSymbol(&code, boa::g_dev_error, sizeof(int))) != cudaSuccess)
+    return pyrc_cuda(h, e, "reading device error word");
+  if (code != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(boa::g_dev_error, &zero, sizeof(int));
+    return pyrc_fail(h, BOA_E_DEVICE, "a coder kernel's copy wait timed out");
+  }
   for (int i = 0; i < h->N; ++i)
     if (sizes_host[i] < 0)
       return pyrc_fail(h, BOA_E_DEVICE, "stream " + std::to_string(i) + " is longer than pitch_words");
@@ -368,13 +565,15 @@ int boa_pyrc_decode_step(boa_pyrc* h, const float* d_probs, int32_t* d_out_symbo
   if (!h || !d_probs || !d_out_symbols) return pyrc_fail(h, BOA_E_INVALID, "null argument");
   cudaSetDevice(h->device);
   cudaStream_t s = (cudaStream_t)stream;
-  switch (pyrc_lanes(h->K)) {
-    case 1: boa::pyrc_launch_dec<1>(d_probs, h->N, h->K, h->words, h->sizes, h->dec, h->pitch, d_out_symbols, d_mask, s); break;
-    case 2: boa::pyrc_launch_dec<2>(d_probs, h->N, h->K, h->words, h->sizes, h->dec, h->pitch, d_out_symbols, d_mask, s); break;
-    case 4: boa::pyrc_launch_dec<4>(d_probs, h->N, h->K, h->words, h->sizes, h->dec, h->pitch, d_out_symbols, d_mask, s); break;
-    case 8: boa::pyrc_launch_dec<8>(d_probs, h->N, h->K, h->words, h->sizes, h->dec, h->pitch, d_out_symbols, d_mask, s); break;
-    case 16: boa::pyrc_launch_dec<16>(d_probs, h->N, h->K, h->words, h->sizes, h->dec, h->pitch, d_out_symbols, d_mask, s); break;
-    default: boa::pyrc_launch_dec<32>(d_probs, h->N, h->K, h->words, h->sizes, h->dec, h->pitch, d_out_symbols, d_mask, s); break;
+  if (pyrc_bulk_ok(h, d_probs)) {
+    const unsigned grid = (unsigned)((h->N + 32 * boa::kBulkWarps - 1) / (32 * boa::kBulkWarps));
+    boa::pyrc_decode_bulk_kernel<<<grid, 32 * boa::kBulkWarps, boa::kPyBulkSmem, s>>>(
+        d_probs, h->N, h->K, h->words, h->sizes, h->dec, h->pitch, d_out_symbols, d_mask);
+  } else {
+    const unsigned grid = (unsigned)((h->N + 32 * boa::kPyWarps - 1) / (32 * boa::kPyWarps));
+    boa::pyrc_decode_kernel<<<grid, 32 * boa::kPyWarps, boa::kPyDecSmem, s>>>(d_probs, h->N, h->K, h->words,
+                                                                             h->sizes, h->dec, h->pitch,
+                                                                             d_out_symbols, d_mask);
   }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? BOA_OK : pyrc_cuda(h, e, "decode step launch");
