@@ -111,12 +111,12 @@ __device__ __forceinline__ void py_encode_update(PyEnc* __restrict__ states, uin
 // decode_step_kernel's search (gpu_range_coder.py:196-201): the first i >= 1
 // with cdf[i] > target (cdf[K] = 2^24 always qualifies); [left, right) =
 // [cdf[i-1], cdf[i]).  `row` holds the K probabilities, bcum the sum P at
-// every 64-entry slab start and `norm` = P_K.  Entries strictly increase when
-// no probability is negative, so the scan starts at the last slab whose
-// first entry is <= target; otherwise it walks every entry from 1 as the
-// reference does.
-__device__ __forceinline__ int py_search(const float* row, const double* bcum, int K, double norm, bool neg,
-                                         uint32_t target, uint32_t& left, uint32_t& right) {
+// entries 0, stride, 2*stride, ... and `norm` = P_K.  Entries strictly
+// increase when no probability is negative, so a binary search over those
+// marks finds the last one <= target and the scan starts there; otherwise it
+// walks every entry from 1 as the reference does.
+__device__ __forceinline__ int py_search(const float* row, const double* bcum, int stride, int K, double norm,
+                                         bool neg, uint32_t target, uint32_t& left, uint32_t& right) {
   const uint32_t free_w = kPyTotal - (uint32_t)K;
   if (!(norm > 0.0) || !isfinite(norm)) {
     const uint32_t step = free_w / (uint32_t)K + 1u;
@@ -126,14 +126,18 @@ __device__ __forceinline__ int py_search(const float* row, const double* bcum, i
     return i;
   }
   const double scale = __ddiv_rn((double)free_w, norm);
-  const int nslab = (K + kSlab - 1) / kSlab;
   int k = 0;
-  if (!neg)
-    for (int kk = 1; kk < nslab; ++kk)
-      if (py_cdf(bcum[kk], scale, (uint32_t)(kk * kSlab)) <= target) k = kk;
+  if (!neg) {
+    int hi = (K + stride - 1) / stride;  // marks k < hi; mark 0 (cdf = 0) always qualifies
+    while (hi - k > 1) {
+      const int mid = (k + hi) >> 1;
+      if (py_cdf(bcum[mid], scale, (uint32_t)(mid * stride)) <= target) k = mid;
+      else hi = mid;
+    }
+  }
   double cc = bcum[k];  // bcum[0] = 0
-  uint32_t prev = py_cdf(cc, scale, (uint32_t)(k * kSlab));
-  for (int j = k * kSlab; j < K; ++j) {
+  uint32_t prev = py_cdf(cc, scale, (uint32_t)(k * stride));
+  for (int j = k * stride; j < K; ++j) {
     cc = __dadd_rn(cc, (double)row[j]);
     const int ii = j + 1;
     const uint32_t v = ii == K ? kPyTotal : py_cdf(cc, scale, (uint32_t)ii);
@@ -240,7 +244,7 @@ __global__ void __launch_bounds__(32 * kPyWarps) pyrc_decode_kernel(const float*
   if (q >= (1ull << 24)) q = (1ull << 24) - 1ull;
   const uint32_t target = (uint32_t)q;
   uint32_t left, right;
-  const int i = py_search(probs + idx * K, bcum, K, c, neg, target, left, right);
+  const int i = py_search(probs + idx * K, bcum, kSlab, K, c, neg, target, left, right);
   out_syms[idx] = i - 1;
   py_decode_update(st, words, sizes, pitch, idx, left, right);
   states[idx] = st;
@@ -256,10 +260,11 @@ __global__ void __launch_bounds__(32 * kPyWarps) pyrc_decode_kernel(const float*
 constexpr int kBulkStride = 260;
 constexpr int kBulkWarps = 2;
 constexpr int kBulkMaxK = 256;
+constexpr int kBulkMark = 16;  // decode: P recorded every 16 entries
 
 struct PyBulkTile {
   float t[32 * kBulkStride];
-  double bcum[32 * (kBulkMaxK / kSlab)];  // decode: P at every 64-entry slab start
+  double bcum[32 * (kBulkMaxK / kBulkMark + 1)];  // decode: P at every 16th entry (row padded: no bank conflicts)
   uint64_t bar;
   uint64_t pad;
 };
@@ -340,11 +345,11 @@ __global__ void __launch_bounds__(32 * kBulkWarps) pyrc_decode_bulk_kernel(const
   if (!active) return;
   const float* row = tl->t + lane * kBulkStride;
   const float4* r4 = reinterpret_cast<const float4*>(row);
-  double* bcum = tl->bcum + lane * (kBulkMaxK / kSlab);
+  double* bcum = tl->bcum + lane * (kBulkMaxK / kBulkMark + 1);
   double c = 0.0;
   bool neg = false;
   for (int q = 0; q < (K >> 2); ++q) {
-    if ((q & (kSlab / 4 - 1)) == 0) bcum[q / (kSlab / 4)] = c;
+    if ((q & (kBulkMark / 4 - 1)) == 0) bcum[q / (kBulkMark / 4)] = c;
     const float4 v = r4[q];
     neg |= v.x < 0.f || v.y < 0.f || v.z < 0.f || v.w < 0.f;
     c = __dadd_rn(c, (double)v.x);
@@ -358,7 +363,7 @@ __global__ void __launch_bounds__(32 * kBulkWarps) pyrc_decode_bulk_kernel(const
   if (q >= (1ull << 24)) q = (1ull << 24) - 1ull;
   const uint32_t target = (uint32_t)q;
   uint32_t left, right;
-  const int i = py_search(row, bcum, K, c, neg, target, left, right);
+  const int i = py_search(row, bcum, kBulkMark, K, c, neg, target, left, right);
   out_syms[idx] = i - 1;
   py_decode_update(st, words, sizes, pitch, idx, left, right);
   states[idx] = st;
