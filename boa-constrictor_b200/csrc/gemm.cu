@@ -373,6 +373,7 @@ __device__ __forceinline__ void load_bias16(const float* b, float (&o)[16]) {
 //               quarter (w - 2) / 4.  LayerNorm moments are combined across
 //               the four column parts in a fixed order.
 constexpr int kEpiWarps = 16;
+constexpr int kMaxPersistN = 2048;  // widest N of a persistent GEMM (d_model 512: 4 * 512)
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kPThreads = 64 + kEpiThreads;
 
@@ -387,7 +388,8 @@ struct PCfg {
   static constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;
   static constexpr int kEpiBuf = kEpiWarps * 32 * kTileStride * 4;  // staging tiles
   static constexpr int kRed = kBM * 4 * 2 * 4;
-  static constexpr int kBudget = 225 * 1024 - 1024 - 256 - kRed - kEpiBuf;
+  static constexpr int kPrm = (kMaxPersistN + 2 * 512) * 4;  // bias [N], ln_w / ln_b [BN <= 512]
+  static constexpr int kBudget = 225 * 1024 - 1024 - 256 - kRed - kEpiBuf - kPrm;
   static constexpr int kStages = kBudget / kStageBytes > 8 ? 8 : kBudget / kStageBytes;
   // N > 256 (LayerNorm over d = 512): 256-wide MMAs side by side in one
   // 512-column accumulator, which then cannot be double-buffered.
@@ -397,7 +399,7 @@ struct PCfg {
   static constexpr int kAccCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : BN <= 256 ? 256 : 512;
   static constexpr int kNumAcc = 2 * kAccCols <= 512 ? 2 : 1;
   static constexpr int kTmemCols = kNumAcc * kAccCols;
-  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256 + kRed + kEpiBuf;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256 + kRed + kEpiBuf + kPrm;
   static_assert(kStages >= 2, "pipeline needs at least two stages");
 };
 
@@ -416,6 +418,9 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* red = reinterpret_cast<float*>(smem + Cfg::kStages * Cfg::kStageBytes + 256);  // [128][4 parts][2]
   float* ebuf = red + kBM * 4 * 2;  // [kEpiWarps][32][kTileStride]
+  float* prm = ebuf + kEpiWarps * 32 * kTileStride;  // bias [N] | ln_w [BN] | ln_b [BN]
+  float* prm_w = prm + kMaxPersistN;
+  float* prm_b = prm_w + 512;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles_n = args.N / BN;
@@ -496,6 +501,15 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       }
     }
   } else {
+    // the epilogue's per-column parameters, staged once per CTA: no chunk
+    // of any tile waits on a global load for them
+    {
+      const int et = threadIdx.x - 64;
+      for (int i = et; i < args.N; i += kEpiThreads) prm[i] = args.bias ? args.bias[i] : 0.f;
+      if (args.ln_w)
+        for (int i = et; i < BN; i += kEpiThreads) { prm_w[i] = args.ln_w[i]; prm_b[i] = args.ln_b[i]; }
+      named_bar_sync(2, kEpiThreads);
+    }
     const int q = warp & 3;
     const int part = (warp - 2) >> 2;  // column quarter 0..3
     const int r_local = q * 32 + lane;
@@ -505,6 +519,29 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
       const int a = it % Cfg::kNumAcc, use = it / Cfg::kNumAcc;
       const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
+      const int c0 = (kChunks * part) / 4 * 16;
+      const int c1 = (kChunks * (part + 1)) / 4 * 16;
+      // RES_LN: this thread's residual row for the first kPre chunks, loaded
+      // while the MMAs still run
+      constexpr int kPre = MODE == EPI_RES_LN ? (kChunks / 4 < 2 ? kChunks / 4 : 2) : 0;
+      float rpre[kPre > 0 ? kPre : 1][16];
+      if constexpr (kPre > 0) {
+        const int grow = m0 + r_local;
+#pragma unroll
+        for (int i = 0; i < kPre; ++i) {
+          if (grow < args.M) {
+            const float4* src = reinterpret_cast<const float4*>(args.res + (size_t)grow * BN + c0 + 16 * i);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float4 t4 = src[j];
+              rpre[i][4 * j] = t4.x; rpre[i][4 * j + 1] = t4.y; rpre[i][4 * j + 2] = t4.z; rpre[i][4 * j + 3] = t4.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) rpre[i][j] = 0.f;
+          }
+        }
+      }
       // only the barrier outcome decides (uniform across the epilogue warps,
       // which then meet at named barriers)
       const bool ok = mbar_wait(&acc_full[a], use & 1);
@@ -514,8 +551,6 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       if (true) { tc_fence_before(); __syncwarp(); if (lane == 0) mbar_arrive(&acc_empty[a]); continue; }
 #endif
       const uint32_t trow = tmem + (uint32_t)(a * Cfg::kAccCols) + ((uint32_t)(q * 32) << 16);
-      const int c0 = (kChunks * part) / 4 * 16;
-      const int c1 = (kChunks * (part + 1)) / 4 * 16;
       float* wb = ebuf + (warp - 2) * 32 * kTileStride;
       const int wrow0 = m0 + q * 32;
       const int nrows = max(0, min(32, args.M - wrow0));
@@ -526,7 +561,7 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           tmem_ld16(trow + c, v);
           if (args.bias) {
             float bb[16];
-            load_bias16(args.bias + n0 + c, bb);
+            load_bias16(prm + n0 + c, bb);
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] += bb[j];
           }
@@ -539,7 +574,7 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           float v[16];
           tmem_ld16(trow + c, v);
           float bb[16];
-          load_bias16(args.bias + n0 + c, bb);
+          load_bias16(prm + n0 + c, bb);
           if (args.act == ACT_GELU) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = apply_act(v[j] + bb[j], ACT_GELU);
@@ -553,17 +588,12 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
       } else {  // EPI_LN_SPLIT / EPI_RES_LN: BN == N, full row in this tile
         float sum = 0.f, sq = 0.f;
-#pragma unroll 1
-        for (int c = c0; c < c1; c += 16) {
+        // pass 1 over one 16-column chunk; r = residual (RES_LN)
+        auto pass1 = [&](int c, const float (&r)[16]) {
           float v[16];
           tmem_ld16(trow + c, v);
-          float r[16];
-          if constexpr (MODE == EPI_RES_LN) {
-            tile_load_f32(wb, lane, args.res + (size_t)wrow0 * BN + c, BN, nrows);
-            tile_get_row(wb, lane, r);
-          }
           float bb[16];
-          load_bias16(args.bias + c, bb);
+          load_bias16(prm + c, bb);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             float x = v[j] + bb[j];
@@ -577,6 +607,21 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             tile_store_f32(wb, lane, args.res + (size_t)wrow0 * BN + c, BN, nrows);
             tmem_st16(trow + c, v);  // keep x in the (consumed) accumulator for pass 2
           }
+        };
+        int cstart = c0;
+        if constexpr (kPre > 0) {
+#pragma unroll
+          for (int i = 0; i < kPre; ++i) pass1(c0 + 16 * i, rpre[i]);
+          cstart = c0 + 16 * kPre;
+        }
+#pragma unroll 1
+        for (int c = cstart; c < c1; c += 16) {
+          float r[16];
+          if constexpr (MODE == EPI_RES_LN) {
+            tile_load_f32(wb, lane, args.res + (size_t)wrow0 * BN + c, BN, nrows);
+            tile_get_row(wb, lane, r);
+          }
+          pass1(c, r);
         }
         if constexpr (MODE == EPI_RES_LN) tmem_st_wait();
         red[(r_local * 4 + part) * 2 + 0] = sum;
@@ -599,14 +644,14 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             // v already holds x = acc + bias + residual (written back to TMEM in pass 1)
           } else {
             float bb[16];
-            load_bias16(args.bias + c, bb);
+            load_bias16(prm + c, bb);
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = v[j] + bb[j];
           }
           if (norm) {
             float lw[16], lb[16];
-            load_bias16(args.ln_w + c, lw);
-            load_bias16(args.ln_b + c, lb);
+            load_bias16(prm_w + c, lw);
+            load_bias16(prm_b + c, lb);
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = (v[j] - mean) * inv_std * lw[j] + lb[j];
           }
@@ -741,6 +786,9 @@ cudaError_t gemm_prepare_device() {
 static int pick_bn(int mode, int N) {
   if ((mode == EPI_LN_SPLIT || mode == EPI_RES_LN) && N == 512) return 512;
   if (mode == EPI_LN_SPLIT || mode == EPI_RES_LN || mode >= EPI_LOGITS) return N;
+#ifdef BOA_BN128
+  if (N % 128 == 0 && N > 128) return 128;
+#endif
   if (N % 256 == 0) return 256;
   if (N % 128 == 0 && N > 128) return 128;  // 384 (GRU gates at d=128)
   if (N % 64 == 0 && N > 128) return 64;    // 192 (GRU gates at d=64)
@@ -750,6 +798,7 @@ static int pick_bn(int mode, int N) {
 cudaError_t gemm_launch(int mode, const __nv_bfloat16* A, long long a_plane, int /*unused*/,
                         const __nv_bfloat16* W, long long w_plane, const GemmArgs& args, cudaStream_t stream) {
   if (args.K % 16 != 0 || args.K <= 0 || args.M <= 0) return cudaErrorInvalidValue;
+  if (mode <= EPI_RES_LN && args.N > kMaxPersistN) return cudaErrorInvalidValue;  // bias staging size
   const int BN = pick_bn(mode, args.N);
   if (BN != 48 && BN != 64 && BN != 128 && BN != 256 && BN != 512) return cudaErrorInvalidValue;
   if (mode >= EPI_LOGITS && BN != 256) return cudaErrorInvalidValue;
