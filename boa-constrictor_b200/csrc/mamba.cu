@@ -178,35 +178,41 @@ __device__ __forceinline__ float ex2_ftz(float x) {
   return y;
 }
 
-// na2 holds A * log2(e) (A = -exp(A_log)), so exp(A dt) = 2^(na2 dt).
+// na2 holds A * log2(e) (A = -exp(A_log)), so exp(A dt) = 2^(na2 dt).  The
+// sixteen states are updated in pairs with packed f32x2 arithmetic; the dt
+// dot product and the sum over states keep two partial sums (even / odd
+// terms), combined once.  Every caller runs this same sequence.
 template <int R>
-__device__ __forceinline__ float scan_update(const float4* __restrict__ dl4, const float (&wdt)[R], float bdt,
-                                             const float (&na2)[16], float (&h)[16], float uv, float z, float dsk) {
+__device__ __forceinline__ float scan_update(const float4* __restrict__ dl4, const float2 (&wdt2)[R / 2], float bdt,
+                                             const float2 (&na2)[8], float2 (&h)[8], float uv, float z, float dsk) {
   // dl4: the row's delta [dt_in(R) | B(16) | C(16)] as aligned float4 (128-bit shared loads)
-  float acc = 0.f;
+  float2 acc2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int k4 = 0; k4 < R / 4; ++k4) {
     const float4 q = dl4[k4];
-    acc = __fmaf_rn(q.x, wdt[4 * k4 + 0], acc);
-    acc = __fmaf_rn(q.y, wdt[4 * k4 + 1], acc);
-    acc = __fmaf_rn(q.z, wdt[4 * k4 + 2], acc);
-    acc = __fmaf_rn(q.w, wdt[4 * k4 + 3], acc);
+    acc2 = ffma2(make_float2(q.x, q.y), wdt2[2 * k4], acc2);
+    acc2 = ffma2(make_float2(q.z, q.w), wdt2[2 * k4 + 1], acc2);
   }
+  const float acc = __fadd_rn(acc2.x, acc2.y);
   const float dt = __logf(__fadd_rn(1.0f, __expf(__fadd_rn(acc, bdt))));  // softplus
   const float dtu = __fmul_rn(dt, uv);
-  float y = 0.f;
+  const float2 dt2 = make_float2(dt, dt), dtu2 = make_float2(dtu, dtu);
+  float2 y2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int n4 = 0; n4 < 4; ++n4) {
     const float4 b4 = dl4[R / 4 + n4], c4 = dl4[R / 4 + 4 + n4];
-    const float bb[4] = {b4.x, b4.y, b4.z, b4.w}, cc[4] = {c4.x, c4.y, c4.z, c4.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = 4 * n4 + j;
-      const float dA = ex2_ftz(__fmul_rn(na2[n], dt));
-      h[n] = __fmaf_rn(dA, h[n], __fmul_rn(bb[j], dtu));
-      y = __fmaf_rn(h[n], cc[j], y);
+    for (int j = 0; j < 2; ++j) {
+      const int p = 2 * n4 + j;
+      const float2 bb = j ? make_float2(b4.z, b4.w) : make_float2(b4.x, b4.y);
+      const float2 cc = j ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
+      const float2 a = fmul2(na2[p], dt2);
+      const float2 dA = make_float2(ex2_ftz(a.x), ex2_ftz(a.y));
+      h[p] = ffma2(dA, h[p], fmul2(bb, dtu2));
+      y2 = ffma2(h[p], cc, y2);
     }
   }
+  float y = __fadd_rn(y2.x, y2.y);
   y = __fmaf_rn(uv, dsk, y);
   return __fmul_rn(y, __fdividef(z, __fadd_rn(1.0f, __expf(-z))));  // y * silu(z)
 }
@@ -229,13 +235,16 @@ __global__ void __launch_bounds__(128, 5) scan_tile_kernel(const float* __restri
   }
   __syncthreads();
   if (c >= di) return;
-  float wdt[R];
+  float2 wdt[R / 2];
 #pragma unroll
-  for (int k = 0; k < R; ++k) wdt[k] = dtw[(size_t)c * R + k];
-  float na[16], h[16];
+  for (int k = 0; k < R / 2; ++k) wdt[k] = reinterpret_cast<const float2*>(dtw + (size_t)c * R)[k];
+  float2 na[8], h[8];
   float* hp = hs + (size_t)b * 16 * di + c;
 #pragma unroll
-  for (int n = 0; n < 16; ++n) { na[n] = negA[(size_t)c * 16 + n]; h[n] = hp[(size_t)n * di]; }
+  for (int p = 0; p < 8; ++p) {
+    na[p] = reinterpret_cast<const float2*>(negA + (size_t)c * 16)[p];
+    h[p] = make_float2(hp[(size_t)(2 * p) * di], hp[(size_t)(2 * p + 1) * di]);
+  }
   const float bdt = dtb[c], dsk = Dv[c];
   // u and z are fetched in batches of 4 positions, one batch ahead, so each
   // thread keeps 8 loads in flight instead of waiting once per position.
@@ -272,7 +281,7 @@ __global__ void __launch_bounds__(128, 5) scan_tile_kernel(const float* __restri
     for (int i = 0; i < PB; ++i) { cu[i] = nu[i]; cz[i] = nz[i]; }
   }
 #pragma unroll
-  for (int n = 0; n < 16; ++n) hp[(size_t)n * di] = h[n];
+  for (int p = 0; p < 8; ++p) { hp[(size_t)(2 * p) * di] = h[p].x; hp[(size_t)(2 * p + 1) * di] = h[p].y; }
 }
 
 // Decompress form (T = 1): persistent CTAs stream each chunk's 16 x di state
@@ -309,13 +318,13 @@ __global__ void __launch_bounds__(1024) scan_step_kernel(const float* __restrict
   const int n_mine = (B - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   if (c == 0)
     for (int s = 0; s < kScanStages && s < n_mine; ++s) issue(s, s);
-  float wdt[R], na[16];
+  float2 wdt[R / 2], na[8];
   float bdt = 0.f, dsk = 0.f;
   if (c < di) {
 #pragma unroll
-    for (int k = 0; k < R; ++k) wdt[k] = dtw[(size_t)c * R + k];
+    for (int k = 0; k < R / 2; ++k) wdt[k] = reinterpret_cast<const float2*>(dtw + (size_t)c * R)[k];
 #pragma unroll
-    for (int n = 0; n < 16; ++n) na[n] = negA[(size_t)c * 16 + n];
+    for (int p = 0; p < 8; ++p) na[p] = reinterpret_cast<const float2*>(negA + (size_t)c * 16)[p];
     bdt = dtb[c];
     dsk = Dv[c];
   }
@@ -330,12 +339,12 @@ __global__ void __launch_bounds__(1024) scan_step_kernel(const float* __restrict
       const float* usm = reinterpret_cast<const float*>(p + st_bytes);
       const float* zsm = usm + di;
       const float4* dl = reinterpret_cast<const float4*>(p + st_bytes + 2 * uz_bytes);
-      float h[16];
+      float2 h[8];
 #pragma unroll
-      for (int n = 0; n < 16; ++n) h[n] = hsm[n * di + c];
+      for (int p = 0; p < 8; ++p) h[p] = make_float2(hsm[(2 * p) * di + c], hsm[(2 * p + 1) * di + c]);
       const float o = scan_update<R>(dl, wdt, bdt, na, h, usm[c], zsm[c], dsk);
 #pragma unroll
-      for (int n = 0; n < 16; ++n) hsm[n * di + c] = h[n];
+      for (int p = 0; p < 8; ++p) { hsm[(2 * p) * di + c] = h[p].x; hsm[(2 * p + 1) * di + c] = h[p].y; }
       __nv_bfloat16 hh, ll;
       split_bf16(o, hh, ll);
       yhl[(size_t)b * di + c] = hh;

@@ -226,6 +226,25 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
 // ---------------------------------------------------------------- bf16 split
 // v = hi + lo with hi = bf16(v), lo = bf16(v - hi): the pair carries ~16
 // significant bits; a*b ~= ah*bh + ah*bl + al*bh to ~2^-16 relative.
+// Packed fp32 pairs (sm_100 f32x2 instructions): each lane of the pair is
+// rounded exactly as the scalar fma.rn / mul.rn / add.rn would round it.
+__device__ __forceinline__ unsigned long long f2_bits(float2 v) {
+  return (unsigned long long)__float_as_uint(v.x) | ((unsigned long long)__float_as_uint(v.y) << 32);
+}
+__device__ __forceinline__ float2 bits_f2(unsigned long long b) {
+  return make_float2(__uint_as_float((unsigned)b), __uint_as_float((unsigned)(b >> 32)));
+}
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return bits_f2(r);
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(r);
+}
+
 __device__ __forceinline__ void split_bf16(float v, __nv_bfloat16& hi, __nv_bfloat16& lo) {
   hi = __float2bfloat16_rn(v);
   lo = __float2bfloat16_rn(v - __bfloat162float(hi));
