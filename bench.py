@@ -85,8 +85,10 @@ def algorithmic_per_launch(cls, B, T, d, L):
     count the three bf16 products of the split-precision GEMM."""
     M, di = B * T, 2 * d
     xp = ((d + 15) // 16 + 32 + 15) // 16 * 16
-    gem = {"in_proj": (d, 4 * d), "x_proj": (di, xp), "out_proj_ln": (di, d), "ff1_gelu": (d, 4 * d),
-           "ff2_res_ln": (4 * d, d), "head1": (d, d), "head2_coder": (d, 256)}
+    gem = {"in_proj": (d, 4 * d), "x_proj": (di, xp), "out_proj_ln": (di, d), "ff2_res_ln": (4 * d, d),
+           "head1": (d, d), "head2_coder": (d, 256)}
+    if cls == "ffn":  # fused feed-forward (both GEMMs) for d <= 256, its first GEMM otherwise
+        return "tensor", 2.0 * 3 * M * (4 * d * d) * (2 if d <= 256 else 1)
     if cls in gem:
         K, N = gem[cls]
         return "tensor", 2.0 * 3 * M * N * K

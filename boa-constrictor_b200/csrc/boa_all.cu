@@ -3,6 +3,7 @@
 // word read back by the host) have exactly one definition without relocatable
 // device code.
 #include "gemm.cu"
+#include "mlp.cu"
 #include "mamba.cu"
 #include "rnn.cu"
 #include "runtime.cpp"

@@ -18,6 +18,7 @@
 // logits and therefore identical CDFs.
 #include <cuda.h>
 #include <cstdio>
+#include <cstring>
 #include <algorithm>
 #include <mutex>
 #include "gemm.cuh"
@@ -405,20 +406,22 @@ struct PCfg {
 
 template <int BN, int MODE>
 __global__ void __launch_bounds__(kPThreads, 1)
-gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, GemmArgs args) {
+gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                    const __grid_constant__ CUtensorMap tmO, GemmArgs args) {
   using Cfg = PCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes);
+  // [stages][epilogue staging (1 KB aligned)][barriers][LN partials][params]
+  float* ebuf = reinterpret_cast<float*>(smem + Cfg::kStages * Cfg::kStageBytes);  // [kEpiWarps][32][kTileStride]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes + Cfg::kEpiBuf);
   uint64_t* full = bars;
   uint64_t* empty = bars + Cfg::kStages;
   uint64_t* acc_full = bars + 2 * Cfg::kStages;       // [2]
   uint64_t* acc_empty = bars + 2 * Cfg::kStages + 2;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * Cfg::kStages + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* red = reinterpret_cast<float*>(smem + Cfg::kStages * Cfg::kStageBytes + 256);  // [128][4 parts][2]
-  float* ebuf = red + kBM * 4 * 2;  // [kEpiWarps][32][kTileStride]
-  float* prm = ebuf + kEpiWarps * 32 * kTileStride;  // bias [N] | ln_w [BN] | ln_b [BN]
+  float* red = reinterpret_cast<float*>(smem + Cfg::kStages * Cfg::kStageBytes + Cfg::kEpiBuf + 256);  // [128][4][2]
+  float* prm = red + kBM * 4 * 2;  // bias [N] | ln_w [BN] | ln_b [BN]
   float* prm_w = prm + kMaxPersistN;
   float* prm_b = prm_w + 512;
 
@@ -434,6 +437,7 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmW);
+    if (MODE == EPI_F32) prefetch_tmap(&tmO);
   }
   if (warp == 1) { tmem_alloc(tmem_slot, Cfg::kTmemCols); tmem_relinquish(); }
   tc_fence_before();
@@ -547,14 +551,18 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       const bool ok = mbar_wait(&acc_full[a], use & 1);
       tc_fence_after();
       if (!ok) break;
-#ifdef BOA_EPI_STUB  // experiment builds only: drain the accumulator without an epilogue
-      if (true) { tc_fence_before(); __syncwarp(); if (lane == 0) mbar_arrive(&acc_empty[a]); continue; }
-#endif
       const uint32_t trow = tmem + (uint32_t)(a * Cfg::kAccCols) + ((uint32_t)(q * 32) << 16);
       float* wb = ebuf + (warp - 2) * 32 * kTileStride;
       const int wrow0 = m0 + q * 32;
       const int nrows = max(0, min(32, args.M - wrow0));
       if constexpr (MODE == EPI_F32) {
+        // Each 32 x 16 chunk leaves through a TMA tensor store: the warp
+        // writes it into its staging tile in the 64-byte-swizzled layout of the
+        // output map (16-byte unit j of row l at unit j ^ ((l >> 1) & 3), so the
+        // 128-bit writes are conflict-free) and lane 0 issues the store.  Rows
+        // past M are clipped by the tensor map.
+        float4* wrow = reinterpret_cast<float4*>(wb) + lane * 4;
+        const int sw = (lane >> 1) & 3;
 #pragma unroll 1
         for (int c = c0; c < c1; c += 16) {
           float v[16];
@@ -565,8 +573,16 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] += bb[j];
           }
-          tile_put_row(wb, lane, v);
-          tile_store_f32(wb, lane, args.out_f32 + (size_t)wrow0 * args.ld_f32 + n0 + c, args.ld_f32, nrows);
+          if (lane == 0) bulk_wait_read_all();  // the previous store has read the tile
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 4; ++j) wrow[j ^ sw] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && nrows > 0) {  // no box wholly past the last row
+            tma_store_2d(&tmO, wb, n0 + c, wrow0);
+            bulk_commit();
+          }
         }
       } else if constexpr (MODE == EPI_ACT_SPLIT) {
 #pragma unroll 1
@@ -666,6 +682,7 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       if (lane == 0) mbar_arrive(&acc_empty[a]);
     }
   }
+  if (MODE == EPI_F32 && warp >= 2 && lane == 0) bulk_wait_all();  // staging tiles stay valid until read
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -707,16 +724,32 @@ static bool make_plane_map(CUtensorMap* map, const void* base, int K, int rows, 
   return r == CUDA_SUCCESS;
 }
 
+// 2-D map over an fp32 [rows][ld] output (the first `cols` columns), box 16 x 32,
+// 64-byte swizzle: the F32 epilogue's tensor stores
+static bool make_out_map_f32(CUtensorMap* map, void* base, int cols, int rows, int ld) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc || !base || ((uintptr_t)base & 15) || (ld * 4) % 16 || cols % 16) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {16, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 static int g_num_sms[64] = {0};
 
 template <int BN, int MODE>
-static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tw, const GemmArgs& a, cudaStream_t st) {
+static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const GemmArgs& a,
+                            cudaStream_t st) {
   if constexpr (MODE <= EPI_RES_LN) {
     int dev = 0;
     cudaGetDevice(&dev);
     const int tiles = (a.N / BN) * ((a.M + kBM - 1) / kBM);
     const int grid = std::min(tiles, g_num_sms[dev & 63] > 0 ? g_num_sms[dev & 63] : 148);
-    gemm_persist_kernel<BN, MODE><<<grid, kPThreads, PCfg<BN>::kSmem, st>>>(ta, tw, a);
+    gemm_persist_kernel<BN, MODE><<<grid, kPThreads, PCfg<BN>::kSmem, st>>>(ta, tw, to, a);
   } else {
     using Cfg = GemmCfg<BN>;
     dim3 grid(a.N / BN, (a.M + kBM - 1) / kBM);
@@ -735,16 +768,16 @@ static cudaError_t set_attr_t() {
 }
 
 template <int BN>
-static cudaError_t dispatch(int mode, const CUtensorMap& ta, const CUtensorMap& tw, const GemmArgs& a,
-                            cudaStream_t st) {
+static cudaError_t dispatch(int mode, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to,
+                            const GemmArgs& a, cudaStream_t st) {
   switch (mode) {
-    case EPI_F32: return launch_t<BN, EPI_F32>(ta, tw, a, st);
-    case EPI_ACT_SPLIT: return launch_t<BN, EPI_ACT_SPLIT>(ta, tw, a, st);
-    case EPI_LN_SPLIT: return launch_t<BN, EPI_LN_SPLIT>(ta, tw, a, st);
-    case EPI_RES_LN: return launch_t<BN, EPI_RES_LN>(ta, tw, a, st);
-    case EPI_LOGITS: return BN == 256 ? launch_t<BN, EPI_LOGITS>(ta, tw, a, st) : cudaErrorInvalidValue;
-    case EPI_HEAD_ENC: return BN == 256 ? launch_t<BN, EPI_HEAD_ENC>(ta, tw, a, st) : cudaErrorInvalidValue;
-    case EPI_HEAD_DEC: return BN == 256 ? launch_t<BN, EPI_HEAD_DEC>(ta, tw, a, st) : cudaErrorInvalidValue;
+    case EPI_F32: return launch_t<BN, EPI_F32>(ta, tw, to, a, st);
+    case EPI_ACT_SPLIT: return launch_t<BN, EPI_ACT_SPLIT>(ta, tw, to, a, st);
+    case EPI_LN_SPLIT: return launch_t<BN, EPI_LN_SPLIT>(ta, tw, to, a, st);
+    case EPI_RES_LN: return launch_t<BN, EPI_RES_LN>(ta, tw, to, a, st);
+    case EPI_LOGITS: return BN == 256 ? launch_t<BN, EPI_LOGITS>(ta, tw, to, a, st) : cudaErrorInvalidValue;
+    case EPI_HEAD_ENC: return BN == 256 ? launch_t<BN, EPI_HEAD_ENC>(ta, tw, to, a, st) : cudaErrorInvalidValue;
+    case EPI_HEAD_DEC: return BN == 256 ? launch_t<BN, EPI_HEAD_DEC>(ta, tw, to, a, st) : cudaErrorInvalidValue;
   }
   return cudaErrorInvalidValue;
 }
@@ -786,9 +819,6 @@ cudaError_t gemm_prepare_device() {
 static int pick_bn(int mode, int N) {
   if ((mode == EPI_LN_SPLIT || mode == EPI_RES_LN) && N == 512) return 512;
   if (mode == EPI_LN_SPLIT || mode == EPI_RES_LN || mode >= EPI_LOGITS) return N;
-#ifdef BOA_BN128
-  if (N % 128 == 0 && N > 128) return 128;
-#endif
   if (N % 256 == 0) return 256;
   if (N % 128 == 0 && N > 128) return 128;  // 384 (GRU gates at d=128)
   if (N % 64 == 0 && N > 128) return 64;    // 192 (GRU gates at d=64)
@@ -804,18 +834,20 @@ cudaError_t gemm_launch(int mode, const __nv_bfloat16* A, long long a_plane, int
   if (mode >= EPI_LOGITS && BN != 256) return cudaErrorInvalidValue;
   // persistent row-parallel modes with BN >= 128 use K-blocks of 32
   const int box_k = (mode <= EPI_RES_LN && BN >= 128) ? 32 : kBK;
-  CUtensorMap ta, tw;
+  CUtensorMap ta, tw, to;
+  std::memset(&to, 0, sizeof(to));
   if (!make_plane_map(&ta, A, args.K, args.M, a_plane, kBM, box_k)) return cudaErrorInvalidValue;
   if (!make_plane_map(&tw, W, args.K, args.N, w_plane, BN > 256 ? 256 : BN, box_k)) return cudaErrorInvalidValue;
+  if (mode == EPI_F32 && !make_out_map_f32(&to, args.out_f32, args.N, args.M, args.ld_f32)) return cudaErrorInvalidValue;
   switch (BN) {
-    case 48: return dispatch<48>(mode, ta, tw, args, stream);
-    case 64: return dispatch<64>(mode, ta, tw, args, stream);
-    case 128: return dispatch<128>(mode, ta, tw, args, stream);
+    case 48: return dispatch<48>(mode, ta, tw, to, args, stream);
+    case 64: return dispatch<64>(mode, ta, tw, to, args, stream);
+    case 128: return dispatch<128>(mode, ta, tw, to, args, stream);
     case 512:
-      if (mode == EPI_LN_SPLIT) return launch_t<512, EPI_LN_SPLIT>(ta, tw, args, stream);
-      if (mode == EPI_RES_LN) return launch_t<512, EPI_RES_LN>(ta, tw, args, stream);
+      if (mode == EPI_LN_SPLIT) return launch_t<512, EPI_LN_SPLIT>(ta, tw, to, args, stream);
+      if (mode == EPI_RES_LN) return launch_t<512, EPI_RES_LN>(ta, tw, to, args, stream);
       return cudaErrorInvalidValue;
-    default: return dispatch<256>(mode, ta, tw, args, stream);
+    default: return dispatch<256>(mode, ta, tw, to, args, stream);
   }
 }
 

@@ -56,6 +56,16 @@ struct PlaneMap;  // opaque TMA descriptor holder (host)
 // contiguous.  a_plane / w_plane: elements between hi and lo planes.
 // BN (CTA tile width) is 256 unless N is small (x_proj: 48).
 cudaError_t gemm_prepare_device();
+
+// The block's feed-forward in one kernel (d_model 64, 128 or 256): with
+// a.N = d, x = a.res [M][d] and xn = the LN2 output (hi/lo planes [2][M][d],
+// xn_plane elements apart), x += W2 . GELU(W1 . xn + b1) + a.bias and then
+// a.out_hl = split(LN(x; a.ln_w, a.ln_b)) (a plain split when a.ln_w is null).
+// W1 [2][4d][d], W2 [2][d][4d] (bf16 hi/lo planes).
+cudaError_t mlp_launch(const __nv_bfloat16* xn, long long xn_plane, const __nv_bfloat16* w1, long long w1_plane,
+                       const __nv_bfloat16* w2, long long w2_plane, const float* b1, const GemmArgs& a,
+                       cudaStream_t stream);
+cudaError_t mlp_prepare_device();
 cudaError_t gemm_launch(int mode, const __nv_bfloat16* A, long long a_plane, int lda_rows,
                         const __nv_bfloat16* W, long long w_plane, const GemmArgs& args,
                         cudaStream_t stream);

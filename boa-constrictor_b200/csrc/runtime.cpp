@@ -198,8 +198,9 @@ enum ProfClass {
   PC_EMBED = 0, PC_IN_PROJ, PC_CONV, PC_X_PROJ, PC_SCAN, PC_OUT_PROJ_LN, PC_FF1, PC_FF2_LN, PC_HEAD1, PC_HEAD2_CODER,
   PC_ENCODE, PC_OTHER
 };
+// "ffn": the fused feed-forward kernel (d <= 256), or its first GEMM (d = 512)
 const char* const kProfNames[BOA_PROF_CLASSES] = {"embed_ln", "in_proj", "conv", "x_proj", "scan", "out_proj_ln",
-                                                  "ff1_gelu", "ff2_res_ln", "head1", "head2_coder", "encode_tile",
+                                                  "ffn", "ff2_res_ln", "head1", "head2_coder", "encode_tile",
                                                   "other"};
 
 cudaEvent_t pool_event(boa_model* m) {
@@ -385,14 +386,21 @@ int forward(boa_model* m, const boa::TokenSrc& src, int B, int T, int head_mode,
       BOA_LAUNCH(PC_SCAN, boa::launch_mingru(m->xz, d, hst, m->u, B, T, st));
       BOA_LAUNCH(PC_OTHER, boa::launch_add_ln(m->x, m->u, d, m->xn, xn_plane, w.ln2w, w.ln2b, M, st));
     }
-    a = boa::GemmArgs{}; a.M = M;
-    a.N = 4 * d; a.K = d; a.bias = w.ff1_b; a.out_hl = hhl; a.ld_hl = 4 * d; a.plane_hl = h_plane;
-    a.act = boa::ACT_GELU;
-    BOA_LAUNCH(PC_FF1, boa::gemm_launch(boa::EPI_ACT_SPLIT, m->xn, xn_plane, 0, w.ff1.p, w.ff1.plane, a, st));
-    a = boa::GemmArgs{}; a.M = M;
-    a.N = d; a.K = 4 * d; a.bias = w.ff2_b; a.res = m->x; a.out_hl = m->xn; a.ld_hl = d; a.plane_hl = xn_plane;
-    if (!last) { a.ln_w = m->layers[l + 1].ln1w; a.ln_b = m->layers[l + 1].ln1b; }
-    BOA_LAUNCH(PC_FF2_LN, boa::gemm_launch(boa::EPI_RES_LN, hhl, h_plane, 0, w.ff2.p, w.ff2.plane, a, st));
+    if (d <= 256) {  // fused feed-forward: the hidden activation stays on chip
+      a = boa::GemmArgs{}; a.M = M;
+      a.N = d; a.bias = w.ff2_b; a.res = m->x; a.out_hl = m->xn; a.ld_hl = d; a.plane_hl = xn_plane;
+      if (!last) { a.ln_w = m->layers[l + 1].ln1w; a.ln_b = m->layers[l + 1].ln1b; }
+      BOA_LAUNCH(PC_FF1, boa::mlp_launch(m->xn, xn_plane, w.ff1.p, w.ff1.plane, w.ff2.p, w.ff2.plane, w.ff1_b, a, st));
+    } else {
+      a = boa::GemmArgs{}; a.M = M;
+      a.N = 4 * d; a.K = d; a.bias = w.ff1_b; a.out_hl = hhl; a.ld_hl = 4 * d; a.plane_hl = h_plane;
+      a.act = boa::ACT_GELU;
+      BOA_LAUNCH(PC_FF1, boa::gemm_launch(boa::EPI_ACT_SPLIT, m->xn, xn_plane, 0, w.ff1.p, w.ff1.plane, a, st));
+      a = boa::GemmArgs{}; a.M = M;
+      a.N = d; a.K = 4 * d; a.bias = w.ff2_b; a.res = m->x; a.out_hl = m->xn; a.ld_hl = d; a.plane_hl = xn_plane;
+      if (!last) { a.ln_w = m->layers[l + 1].ln1w; a.ln_b = m->layers[l + 1].ln1b; }
+      BOA_LAUNCH(PC_FF2_LN, boa::gemm_launch(boa::EPI_RES_LN, hhl, h_plane, 0, w.ff2.p, w.ff2.plane, a, st));
+    }
   }
   if (m->backbone != BOA_BACKBONE_MAMBA)
     BOA_LAUNCH(PC_OTHER, boa::launch_rms_split(m->x, d, m->final_norm, m->xn, xn_plane, M, st));
@@ -660,7 +668,8 @@ int boa_model_load(const char* path, int backbone, int d, int nl, int device, bo
   }
   if (fnorm >= 0) m->final_norm = fp[fnorm];
   m->h1 = hp[h1]; m->h1_b = fp[h1b]; m->h2 = hp[h2]; m->h2_b = fp[h2b];
-  if ((e = boa::gemm_prepare_device()) != cudaSuccess || (e = boa::scan_prepare_device()) != cudaSuccess)
+  if ((e = boa::gemm_prepare_device()) != cudaSuccess || (e = boa::scan_prepare_device()) != cudaSuccess ||
+      (e = boa::mlp_prepare_device()) != cudaSuccess)
     return fail(nullptr, BOA_E_CUDA, std::string("GEMM kernel setup: ") + cudaGetErrorString(e));
   if ((e = cudaStreamCreateWithFlags(&m->own, cudaStreamNonBlocking)) != cudaSuccess ||
       (e = cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming)) != cudaSuccess ||
