@@ -104,10 +104,10 @@ def algorithmic_per_launch(cls, B, T, d, L):
     return None, 0.0
 
 
-# DRAM bytes (read + write) of one launch from `ncu --set full`, recorded in
-# profiles/ncu_launches_small_roundtrip.md, per chunk of the batch (the
+# DRAM bytes (read + write) of one launch from `ncu --set full` (the
+# small-round-trip capture summarised under profiles/), per chunk of the batch (the
 # kernel's traffic scales with the number of chunks): decompress-step scan.
-NCU_TRAFFIC_PER_CHUNK = {("scan", "decode"): (608.086784e6 + 523.836672e6) / 16384}
+NCU_TRAFFIC_PER_CHUNK = {("scan", "decode"): (609.040384e6 + 524.623360e6) / 16384}
 
 
 # --------------------------------------------------------------------------- clocks
