@@ -350,7 +350,8 @@ def main():
     dist = None
     if ws > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo")
+        dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo",
+                                device_id=torch.device("cuda", local) if torch.cuda.is_available() else None)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     boa = __import__("__graft_entry__").load_package()
