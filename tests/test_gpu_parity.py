@@ -40,6 +40,22 @@ def test_rc_encode_cdf_bit_exact(boa, oracle, m64, n_streams, n_steps):
     assert np.array_equal(back, syms)
 
 
+@pytest.mark.parametrize("n_streams,n_steps", [(65536, 4), (4, 65536)])
+def test_rc_configs1_geometry_bit_exact(boa, oracle, m64, n_streams, n_steps):
+    """configs[1]'s two dimensions: its full stream count (65,536 streams) and
+    its full stream length (65,536 symbols), Dirichlet(0.1) integer CDFs; every
+    stream word-exact against the CPU coder and decoded back."""
+    rng = np.random.default_rng(n_streams + 7 * n_steps)
+    Q, syms = dirichlet_cdfs(rng, n_steps, n_streams)
+    sizes, pay = m64.rc_encode_cdf(Q, syms)
+    o = 0
+    for s in range(n_streams):
+        ref = oracle.rc_encode_cdf(Q[:, s], syms[:, s])
+        assert sizes[s] == ref.size and np.array_equal(pay[o:o + sizes[s]], ref), s
+        o += int(sizes[s])
+    assert np.array_equal(m64.rc_decode_cdf(Q, sizes, pay), syms)
+
+
 def test_rc_frequency_one_symbols(boa, oracle, m64):
     n = 500
     Q = np.zeros((n, 2, 257), np.uint32)
