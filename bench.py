@@ -18,8 +18,8 @@ value  = MB/s (2^20 B) of input round-tripped per second, whole job, inputs
 e2e    = the same through the host-buffer C-ABI calls (boa_compress_chunks /
          boa_decompress_chunks) from pinned host memory, copies included.
 --impl reference times the CPU restatement of the reference path on this
-host's cores (the reference ships no CPU C++ path; its CUDA binary is timed
-separately).
+host's cores (the reference ships no CPU C++ path; its CUDA binary was timed
+separately through its own CLI).
 """
 from __future__ import annotations
 

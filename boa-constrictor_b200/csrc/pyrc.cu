@@ -439,7 +439,7 @@ struct boa_pyrc {
   int32_t* sizes = nullptr;
   std::string err;
   ~boa_pyrc() {
-    if (arena) { cudaSetDevice(device); cudaFree(arena); }
+    if (arena) { DeviceGuard dev(device); cudaFree(arena); }
   }
 };
 
@@ -466,8 +466,11 @@ int boa_pyrc_create(int n_streams, int vocab, int pitch_words, int device, boa_p
     return pyrc_fail(nullptr, BOA_E_INVALID, "need n_streams > 0, 1 <= vocab <= 1024 and pitch_words > 0");
   std::unique_ptr<boa_pyrc> h(new boa_pyrc());
   h->device = device; h->N = n_streams; h->K = vocab; h->pitch = pitch_words;
-  cudaError_t e = cudaSetDevice(device);
-  if (e != cudaSuccess) return pyrc_cuda(nullptr, e, "cudaSetDevice");
+  int n_dev = 0;
+  cudaError_t e = cudaGetDeviceCount(&n_dev);
+  if (e != cudaSuccess) return pyrc_cuda(nullptr, e, "cudaGetDeviceCount");
+  if (device < 0 || device >= n_dev) return pyrc_fail(nullptr, BOA_E_CUDA, "no CUDA device " + std::to_string(device));
+  DeviceGuard dev(device);
   if ((e = boa::pyrc_prepare()) != cudaSuccess) return pyrc_cuda(nullptr, e, "coder kernel setup");
   auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
   const size_t N = (size_t)n_streams;
@@ -496,7 +499,7 @@ const char* boa_pyrc_last_error(const boa_pyrc* h) { return h ? h->err.c_str() :
 int boa_pyrc_encode_step(boa_pyrc* h, const int32_t* d_symbols, const float* d_probs, const uint8_t* d_mask,
                          void* stream) {
   if (!h || !d_symbols || !d_probs) return pyrc_fail(h, BOA_E_INVALID, "null argument");
-  cudaSetDevice(h->device);
+  DeviceGuard dev(h->device);
   cudaStream_t s = (cudaStream_t)stream;
   if (pyrc_bulk_ok(h, d_probs)) {
     const unsigned grid = (unsigned)((h->N + 32 * boa::kBulkWarps - 1) / (32 * boa::kBulkWarps));
@@ -513,7 +516,7 @@ int boa_pyrc_encode_step(boa_pyrc* h, const int32_t* d_symbols, const float* d_p
 
 int boa_pyrc_finalize(boa_pyrc* h, void* stream) {
   if (!h) return BOA_E_INVALID;
-  cudaSetDevice(h->device);
+  DeviceGuard dev(h->device);
   boa::pyrc_finalize_kernel<<<(unsigned)((h->N + 127) / 128), 128, 0, (cudaStream_t)stream>>>(h->enc, h->words, h->sizes,
                                                                                               h->N, h->pitch);
   cudaError_t e = cudaGetLastError();
@@ -522,7 +525,7 @@ int boa_pyrc_finalize(boa_pyrc* h, void* stream) {
 
 int boa_pyrc_read(boa_pyrc* h, uint32_t* words_host, int32_t* sizes_host, void* stream) {
   if (!h || !sizes_host) return pyrc_fail(h, BOA_E_INVALID, "null argument");
-  cudaSetDevice(h->device);
+  DeviceGuard dev(h->device);
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e = cudaMemcpyAsync(sizes_host, h->sizes, (size_t)h->N * 4, cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess && words_host)
@@ -548,7 +551,7 @@ int boa_pyrc_load(boa_pyrc* h, const uint32_t* words_host, const int32_t* sizes_
   for (int i = 0; i < h->N; ++i)
     if (sizes_host[i] < 0 || sizes_host[i] > h->pitch)
       return pyrc_fail(h, BOA_E_INVALID, "stream " + std::to_string(i) + " exceeds pitch_words");
-  cudaSetDevice(h->device);
+  DeviceGuard dev(h->device);
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e = cudaMemcpyAsync(h->words, words_host, (size_t)h->N * h->pitch * 4, cudaMemcpyHostToDevice, s);
   if (e == cudaSuccess) e = cudaMemcpyAsync(h->sizes, sizes_host, (size_t)h->N * 4, cudaMemcpyHostToDevice, s);
@@ -558,7 +561,7 @@ int boa_pyrc_load(boa_pyrc* h, const uint32_t* words_host, const int32_t* sizes_
 
 int boa_pyrc_init_decoder(boa_pyrc* h, void* stream) {
   if (!h) return BOA_E_INVALID;
-  cudaSetDevice(h->device);
+  DeviceGuard dev(h->device);
   boa::pyrc_init_dec_kernel<<<(unsigned)((h->N + 127) / 128), 128, 0, (cudaStream_t)stream>>>(h->words, h->sizes, h->dec,
                                                                                               h->N, h->pitch);
   cudaError_t e = cudaGetLastError();
@@ -568,7 +571,7 @@ int boa_pyrc_init_decoder(boa_pyrc* h, void* stream) {
 int boa_pyrc_decode_step(boa_pyrc* h, const float* d_probs, int32_t* d_out_symbols, const uint8_t* d_mask,
                          void* stream) {
   if (!h || !d_probs || !d_out_symbols) return pyrc_fail(h, BOA_E_INVALID, "null argument");
-  cudaSetDevice(h->device);
+  DeviceGuard dev(h->device);
   cudaStream_t s = (cudaStream_t)stream;
   if (pyrc_bulk_ok(h, d_probs)) {
     const unsigned grid = (unsigned)((h->N + 32 * boa::kBulkWarps - 1) / (32 * boa::kBulkWarps));

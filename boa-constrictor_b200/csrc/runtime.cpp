@@ -28,6 +28,23 @@ namespace {
 
 std::string g_load_error;  // boa_model_load failures (no handle yet)
 
+// Makes `device` current for the scope of an API call and restores the
+// caller's current device afterwards: no entry point changes it.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int device) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != device) cudaSetDevice(device);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+};
+
+
 struct HL {  // bf16 hi/lo weight planes, [2][N][K]
   bf16* p = nullptr;
   long long plane = 0;
@@ -164,7 +181,7 @@ struct boa_model {
 };
 
 boa_model::~boa_model() {
-  cudaSetDevice(device);
+  DeviceGuard dev(device);
   if (own) cudaStreamSynchronize(own);
   for (auto& p : pending) { cudaEventDestroy(p.a); cudaEventDestroy(p.b); }
   for (auto e : ev_pool) cudaEventDestroy(e);
@@ -233,11 +250,11 @@ struct Launch {
     BOA_CK(call);                \
   } while (0)
 
-// Entry / exit ordering with an external stream.
+// Entry / exit ordering with an external stream (and the handle's device).
 struct StreamScope {
   boa_model* m;
-  explicit StreamScope(boa_model* mm) : m(mm) {
-    cudaSetDevice(m->device);
+  DeviceGuard dev;
+  explicit StreamScope(boa_model* mm) : m(mm), dev(mm->device) {
     if (m->has_ext) { cudaEventRecord(m->ev_in, m->ext); cudaStreamWaitEvent(m->own, m->ev_in, 0); }
   }
   ~StreamScope() {
@@ -620,8 +637,12 @@ int boa_model_load(const char* path, int backbone, int d, int nl, int device, bo
                     " (parsed " + std::to_string(R.off) + " of " + std::to_string(R.buf.size()) + " bytes)");
 
   // ---- upload into one arena
-  cudaError_t e = cudaSetDevice(device);
-  if (e != cudaSuccess) return fail(nullptr, BOA_E_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+  int n_dev = 0;
+  cudaError_t e = cudaGetDeviceCount(&n_dev);
+  if (e != cudaSuccess || device < 0 || device >= n_dev)
+    return fail(nullptr, BOA_E_CUDA, std::string("no CUDA device ") + std::to_string(device) +
+                                         (e != cudaSuccess ? std::string(": ") + cudaGetErrorString(e) : ""));
+  DeviceGuard dev(device);
   auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
   size_t total = al(emb.size() * 4);
   for (auto& v : f32s) total += al(v.size() * 4);
@@ -715,7 +736,7 @@ uint64_t boa_device_bytes(const boa_model* m) {
 
 int boa_sync(boa_model* m) {
   if (!m) return BOA_E_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dev(m->device);
   BOA_CK(cudaStreamSynchronize(m->own));
   if (m->has_ext) BOA_CK(cudaStreamSynchronize(m->ext));
   return read_dev_error(m);
@@ -940,7 +961,7 @@ int boa_profile_read(boa_model* m, int c, double* total_ms, uint64_t* n) {
   if (!m) return BOA_E_INVALID;
   if (c < 0 || c >= BOA_PROF_CLASSES) return fail(m, BOA_E_INVALID, "kernel class out of range");
   if (!m->pending.empty()) {
-    cudaSetDevice(m->device);
+    DeviceGuard dev(m->device);
     BOA_CK(cudaStreamSynchronize(m->own));
     for (auto& p : m->pending) {
       float ms = 0.f;

@@ -48,6 +48,8 @@ typedef struct boa_model boa_model;
  * file size must match the dims exactly (BOA_E_FORMAT otherwise). */
 int boa_model_load(const char* weights_path, int backbone, int d_model, int n_layers, int device,
                    boa_model** out);
+/* Every call on a handle runs on the handle's device and leaves the calling
+ * thread's current CUDA device as it found it. */
 /* Releases the handle and all its device memory (the reference never frees). */
 void boa_model_free(boa_model* h);
 /* Message of the last failed call on this handle (or of the last failed
@@ -105,7 +107,11 @@ int boa_compress_device(boa_model* h, const uint8_t* d_data, uint64_t n_bytes, u
 int boa_decompress_device(boa_model* h, const uint32_t* d_payload, const uint64_t* d_offsets,
                           const uint32_t* d_sizes_words, const uint8_t* d_first_bytes, uint64_t n_bytes,
                           uint32_t chunk_len, uint32_t n_chunks, uint8_t* d_out);
-/* Waits for the handle's work and reports device-side failures. */
+/* Waits for the handle's work and reports device-side failures
+ * (BOA_E_DEVICE).  Kernels record such a failure -- a bounded wait that ran
+ * out, a stream longer than its capacity -- in one error word per device,
+ * which this call reads and clears: with several handles on one device, a
+ * failure is reported to whichever handle synchronises first. */
 int boa_sync(boa_model* h);
 /* Device memory the handle holds (weights + work buffers + states). */
 uint64_t boa_device_bytes(const boa_model* h);

@@ -7,8 +7,8 @@
 #   _gpu_range_cuda_ext*.so  the Python codec's batch range coder: importing
 #                    gpu_range_coder.py compiles it (gpu_range_coder.py:14-367);
 #                    TMPDIR points its build folder into _ref
-# Needs the reference checkout (default /root/reference, or $BOA_REF_DIR);
-# without it the script does nothing and says so.  Outputs are git-ignored.
+# Needs the reference checkout ($BOA_REF_DIR, or the default below); without
+# it the script does nothing and says so.  Outputs are git-ignored.
 set -euo pipefail
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
 REF="${BOA_REF_DIR:-/root/reference}/portability_solved_cpp"
