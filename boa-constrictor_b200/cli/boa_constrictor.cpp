@@ -9,8 +9,9 @@
 // Defaults follow the reference: d_model 256, n_layers 1, chunk 4096.  The
 // extra --gpus N shards the chunks over N GPUs of this node (contiguous chunk
 // ranges, one host thread and one library handle per GPU); the container is
-// the same BOA2 file either way.  --warm-start is not supported yet and is
-// rejected rather than silently ignored.
+// the same BOA2 file either way.  --warm-start (one GPU only) runs W lanes
+// that carry the model state from each chunk into the next one of the same
+// lane (boa.cpp:313-319); the container records W for decompress.
 #include <algorithm>
 #include <chrono>
 #include <cstdio>
@@ -197,7 +198,7 @@ int main(int argc, char** argv) {
   if (argc < 5) {
     std::cerr << "Usage: boa_constrictor <compress|decompress> <model> <input> <output> [d_model] [n_layers] "
                  "[--backbone mamba|lstm|gru|mingru] [--gpu-batch B] [--max-chunks C] [--chunk-size S] [--tile T] "
-                 "[--temperature T] [--show-timings] [--no-graph] [--gpus N]\n";
+                 "[--temperature T] [--show-timings] [--no-graph] [--gpus N] [--warm-start]\n";
     return 1;
   }
   Opts o;

@@ -92,8 +92,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN;
-  const int m0 = blockIdx.y * kBM;
+  const int n0 = blockIdx.y * BN;   // row tiles on x: up to 2^31 - 1 of them (y stops at 65535)
+  const int m0 = blockIdx.x * kBM;
   const int nkb = (args.K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -752,7 +752,7 @@ static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tw, const 
     gemm_persist_kernel<BN, MODE><<<grid, kPThreads, PCfg<BN>::kSmem, st>>>(ta, tw, to, a);
   } else {
     using Cfg = GemmCfg<BN>;
-    dim3 grid(a.N / BN, (a.M + kBM - 1) / kBM);
+    dim3 grid((a.M + kBM - 1) / kBM, a.N / BN);
     gemm_kernel<BN, MODE><<<grid, kThreads, Cfg::kSmem, st>>>(ta, tw, a);
   }
   return cudaGetLastError();

@@ -226,8 +226,8 @@ __global__ void __launch_bounds__(128, 5) scan_tile_kernel(const float* __restri
                                                         const float* __restrict__ xz, int di, float* __restrict__ hs,
                                                         __nv_bfloat16* __restrict__ yhl, long long plane, int T) {
   extern __shared__ float sdelta[];  // [T][ld]
-  const int b = blockIdx.y;
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = blockIdx.x;  // chunks on x (y stops at 65535)
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
   {
     const float4* src = reinterpret_cast<const float4*>(delta + (size_t)b * T * ld);
     float4* dst = reinterpret_cast<float4*>(sdelta);
@@ -391,7 +391,7 @@ cudaError_t launch_scan(const float* delta, int ld, int r, const float* dtw, con
     }
     return cudaGetLastError();
   }
-  dim3 block(128), grid((di + 127) / 128, B);
+  dim3 block(128), grid(B, (di + 127) / 128);
   const size_t sm = (size_t)T * ld * sizeof(float);
   if (sm > 200 * 1024 || (T * ld) % 4) return cudaErrorInvalidValue;
   switch (r) {
