@@ -104,6 +104,35 @@ def algorithmic_per_launch(cls, B, T, d, L):
     return None, 0.0
 
 
+def step_roofline(d, L, B, T, hbm_gbs, tf_sust):
+    """Roofline of one compress tile (B chunks x T positions) and one decode
+    step (B chunks x 1 position): the slower of the algorithmic GEMM FLOPs at
+    the sustained bf16 tensor peak and the weight + recurrent-state bytes at
+    the HBM copy peak.  FLOPs are the fp32 model's (the three bf16 products of
+    the split-precision GEMMs are not counted); state is conv [3][di] + ssm
+    [16][di] fp32 per layer, read and written once per tile or step."""
+    di = 2 * d
+    r = (d + 15) // 16
+    xp = ((r + 32 + 15) // 16) * 16
+    gemm_kn = [(d, 2 * di), (di, xp), (r, di), (di, d), (d, 4 * d), (4 * d, d)]
+    flops_per_byte = L * sum(2 * k * n for k, n in gemm_kn) + 2 * (d * d + d * 256)
+    weight_bytes = 4 * (L * sum(k * n for k, n in gemm_kn) + d * d + d * 256 + 256 * d)
+    state_per_chunk = L * (16 + 3) * di * 4
+
+    def one(tokens_per_chunk):
+        byts = 2 * state_per_chunk * B + weight_bytes + 2 * B * tokens_per_chunk
+        t_mem = byts / (hbm_gbs * 1e9)
+        t_flop = flops_per_byte * B * tokens_per_chunk / (tf_sust * 1e12)
+        return max(t_mem, t_flop), ("hbm" if t_mem >= t_flop else "tensor")
+
+    tc, bc = one(T)
+    td, bd = one(1)
+    return {"compress_bound_MBps": B * T / MiB / tc, "compress_bound": bc,
+            "decompress_bound_MBps": B / MiB / td, "decompress_bound": bd,
+            "flops_per_byte": flops_per_byte, "state_bytes_per_chunk": state_per_chunk,
+            "weight_bytes": weight_bytes}
+
+
 # DRAM bytes (read + write) of one launch from `ncu --set full` (the
 # small-round-trip capture summarised under profiles/), per chunk of the batch (the
 # kernel's traffic scales with the number of chunks): decompress-step scan.
@@ -514,6 +543,10 @@ def main():
 
     if rank == 0:
         total = n * ws
+        step_rl = step_roofline(a.d_model, a.layers, C, T, hbm_peak, tf_sust)
+        step_rl["compress_frac"] = (n / MiB / (comp_ms * 1e-3)) / step_rl["compress_bound_MBps"]
+        step_rl["decompress_frac"] = (n / MiB / (dec_ms * 1e-3)) / step_rl["decompress_bound_MBps"]
+        step_rl["peaks"] = f"{peak_kind}: HBM copy {hbm_peak} GB/s, bf16 sustained {tf_sust} TFLOP/s"
         line = {
             "metric": "compress+decompress round-trip MB/s",
             "value": total / MiB / (step_ms * 1e-3),
@@ -533,6 +566,7 @@ def main():
                          "traffic": (NCU_TRAFFIC_PER_CHUNK[(dom, "decode")] * C
                                      if in_decode and (dom, "decode") in NCU_TRAFFIC_PER_CHUNK else None),
                          "peak_source": f"{peak_kind} ({'bf16 sustained' if bound == 'tensor' else 'HBM copy'})"},
+            "step_roofline": step_rl,
             "kernels": kern,
             "cpu_baseline": cpu,
             "e2e": {"value": total / MiB / (e2e_step_ms * 1e-3), "unit": "MB/s",
