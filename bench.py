@@ -553,10 +553,15 @@ def main():
             "unit": "MB/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup, "ms_per_step": step_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16x3 (fp32-accurate)",
             "data": "synthetic: seeded float32 particle records, random-init weights",
-            "config": {"workload": "configs[2]: mamba d256 L8, 16384 chunks x 16 KiB = 256 MiB per GPU, one batch",
+            "config": {"workload": (f"{'configs[2]: ' if (a.d_model, a.layers, C, S) == (256, 8, 16384, 16384) else ''}"
+                                    f"mamba d{a.d_model} L{a.layers}, {C} chunks x {S} B = {n / MiB:g} MiB per GPU, "
+                                    "one batch"),
                        "d_model": a.d_model, "n_layers": a.layers, "chunks_per_gpu": C, "chunk_len": S,
                        "batch_chunks": C, "compress_tile": T, "parallelism": f"chunk-sharded x{ws}",
-                       "l2": "inputs (256 MiB) and recurrent state (5 GiB) exceed L2; no flush needed",
+                       "l2": (f"inputs ({n / MiB:g} MiB) and recurrent state "
+                              f"({C * a.layers * 19 * 2 * a.d_model * 4 / MiB / 1024:.2f} GiB) "
+                              + ("exceed L2 (126 MB); no flush needed" if n > 126e6 else
+                                 "state exceeds L2 (126 MB), inputs do not; no flush")),
                        "warmup": f"{a.warmup} round trips of the same chunks truncated to {wl} B"},
             "compress_MBps": total / MiB / (comp_ms * 1e-3),
             "decompress_MBps": total / MiB / (dec_ms * 1e-3),
