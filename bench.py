@@ -561,7 +561,9 @@ def main():
                        "l2": (f"inputs ({n / MiB:g} MiB) and recurrent state "
                               f"({C * a.layers * 19 * 2 * a.d_model * 4 / MiB / 1024:.2f} GiB) "
                               + ("exceed L2 (126 MB); no flush needed" if n > 126e6 else
-                                 "state exceeds L2 (126 MB), inputs do not; no flush")),
+                                 "state exceeds L2 (126 MB), inputs do not; no flush"
+                                 if C * a.layers * 19 * 2 * a.d_model * 4 > 126e6 else
+                                 "fit in L2 (126 MB): warm-cache timing, not a headline number")),
                        "warmup": f"{a.warmup} round trips of the same chunks truncated to {wl} B"},
             "compress_MBps": total / MiB / (comp_ms * 1e-3),
             "decompress_MBps": total / MiB / (dec_ms * 1e-3),
