@@ -380,12 +380,15 @@ constexpr int kPThreads = 64 + kEpiThreads;
 
 // K-block of 32 (64-byte rows, 64-byte swizzle) for wide tiles so four or more
 // stages fit and cover TMA latency; 64 (128-byte swizzle) for narrow ones.
-template <int BN>
+// PAIR: a cluster of two CTAs computes a 256-row tile with cta_group::2
+// MMAs; each CTA stages its 128 rows of A and half of the tile's W rows.
+template <int BN, bool PAIR = false>
 struct PCfg {
   static constexpr int kBK = BN >= 128 ? 32 : 64;
   static constexpr int kSwz = kBK * 2;  // swizzle span in bytes (64 or 128)
   static constexpr int kABytes = kBM * kBK * 2;
-  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kBBytes = (PAIR ? BN / 2 : BN) * kBK * 2;
+  static constexpr int kTileRows = PAIR ? 2 * kBM : kBM;
   static constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;
   static constexpr int kEpiBuf = kEpiWarps * 32 * kTileStride * 4;  // staging tiles
   static constexpr int kRed = kBM * 4 * 2 * 4;
@@ -396,7 +399,7 @@ struct PCfg {
   // 512-column accumulator, which then cannot be double-buffered.
   static constexpr int kMmaN = BN > 256 ? 256 : BN;
   static constexpr int kNSub = BN / kMmaN;
-  static constexpr int kBoxRows = kMmaN;
+  static constexpr int kBoxRows = PAIR ? kMmaN / 2 : kMmaN;  // W rows this CTA stages per MMA
   static constexpr int kAccCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : BN <= 256 ? 256 : 512;
   static constexpr int kNumAcc = 2 * kAccCols <= 512 ? 2 : 1;
   static constexpr int kTmemCols = kNumAcc * kAccCols;
@@ -404,11 +407,11 @@ struct PCfg {
   static_assert(kStages >= 2, "pipeline needs at least two stages");
 };
 
-template <int BN, int MODE>
+template <int BN, int MODE, bool PAIR = false>
 __global__ void __launch_bounds__(kPThreads, 1)
 gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                     const __grid_constant__ CUtensorMap tmO, GemmArgs args) {
-  using Cfg = PCfg<BN>;
+  using Cfg = PCfg<BN, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // [stages][epilogue staging (1 KB aligned)][barriers][LN partials][params]
@@ -427,55 +430,90 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles_n = args.N / BN;
-  const int n_tiles = n_tiles_n * ((args.M + kBM - 1) / kBM);
+  const int n_tiles = n_tiles_n * ((args.M + Cfg::kTileRows - 1) / Cfg::kTileRows);
   const int nkb = (args.K + Cfg::kBK - 1) / Cfg::kBK;
+  // tile walk: one per CTA, or one per CTA pair (rank 0 issues the MMAs)
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const int t_first = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int t_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int row_off = (int)rank * kBM;  // this CTA's rows within the tile
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int a = 0; a < 2; ++a) { mbar_init(&acc_full[a], 1); mbar_init(&acc_empty[a], kEpiWarps); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&acc_full[a], 1); mbar_init(&acc_empty[a], (PAIR ? 2 : 1) * kEpiWarps); }
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmW);
     if (MODE == EPI_F32) prefetch_tmap(&tmO);
   }
-  if (warp == 1) { tmem_alloc(tmem_slot, Cfg::kTmemCols); tmem_relinquish(); }
+  if (warp == 1) {
+    if constexpr (PAIR) { tmem_alloc_pair(tmem_slot, Cfg::kTmemCols); tmem_relinquish_pair(); }
+    else { tmem_alloc(tmem_slot, Cfg::kTmemCols); tmem_relinquish(); }
+  }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // pair: the MMA issuer signals a barrier in both CTAs; everyone else signals rank 0's
+  auto commit_both = [&](uint64_t* bar) {
+    if constexpr (PAIR) { umma_commit_pair(cluster_addr(bar, 0)); umma_commit_pair(cluster_addr(bar, 1)); }
+    else umma_commit(bar);
+  };
 
   if (warp == 0) {
     if (lane == 0) {
       int g = 0;  // global k-block counter (stage / phase)
-      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
-        const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
+      for (int t = t_first; t < n_tiles && !*abort_flag; t += t_step) {
+        const int m0 = (t / n_tiles_n) * Cfg::kTileRows + row_off, n0 = (t % n_tiles_n) * BN;
         for (int kb = 0; kb < nkb; ++kb, ++g) {
           const int s = g % Cfg::kStages;
           if (g >= Cfg::kStages && !mbar_wait(&empty[s], ((g / Cfg::kStages) - 1) & 1)) { *abort_flag = 1; break; }
           uint8_t* st = smem + s * Cfg::kStageBytes;
-          mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
           const int k0 = kb * Cfg::kBK;
-          tma_load_3d(st, &tmA, &full[s], k0, m0, 0);
-          tma_load_3d(st + Cfg::kABytes, &tmA, &full[s], k0, m0, 1);
+          if constexpr (PAIR) {
+            // both CTAs' bytes land on rank 0's barrier, which rank 0 arms for both
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
+            const uint32_t fb = cluster_addr(&full[s], 0);
+            tma_load_3d_pair(st, &tmA, fb, k0, m0, 0);
+            tma_load_3d_pair(st + Cfg::kABytes, &tmA, fb, k0, m0, 1);
 #pragma unroll
-          for (int sub = 0; sub < Cfg::kNSub; ++sub) {
-            const int off = sub * Cfg::kBoxRows * Cfg::kBK * 2;
-            tma_load_3d(st + 2 * Cfg::kABytes + off, &tmW, &full[s], k0, n0 + sub * Cfg::kBoxRows, 0);
-            tma_load_3d(st + 2 * Cfg::kABytes + Cfg::kBBytes + off, &tmW, &full[s], k0, n0 + sub * Cfg::kBoxRows, 1);
+            for (int sub = 0; sub < Cfg::kNSub; ++sub) {
+              const int off = sub * Cfg::kBoxRows * Cfg::kBK * 2;
+              const int wr = n0 + sub * Cfg::kMmaN + (int)rank * Cfg::kBoxRows;
+              tma_load_3d_pair(st + 2 * Cfg::kABytes + off, &tmW, fb, k0, wr, 0);
+              tma_load_3d_pair(st + 2 * Cfg::kABytes + Cfg::kBBytes + off, &tmW, fb, k0, wr, 1);
+            }
+          } else {
+            mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+            tma_load_3d(st, &tmA, &full[s], k0, m0, 0);
+            tma_load_3d(st + Cfg::kABytes, &tmA, &full[s], k0, m0, 1);
+#pragma unroll
+            for (int sub = 0; sub < Cfg::kNSub; ++sub) {
+              const int off = sub * Cfg::kBoxRows * Cfg::kBK * 2;
+              tma_load_3d(st + 2 * Cfg::kABytes + off, &tmW, &full[s], k0, n0 + sub * Cfg::kBoxRows, 0);
+              tma_load_3d(st + 2 * Cfg::kABytes + Cfg::kBBytes + off, &tmW, &full[s], k0, n0 + sub * Cfg::kBoxRows, 1);
+            }
           }
         }
       }
+      if constexpr (PAIR) {
+        // the MMA issuer's last commits to this CTA's empty barriers land
+        // before the CTA may exit
+        for (int i = g > Cfg::kStages ? g - Cfg::kStages : 0; i < g; ++i)
+          if (!mbar_wait(&empty[i % Cfg::kStages], (i / Cfg::kStages) & 1)) break;
+      }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(kBM, Cfg::kMmaN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(Cfg::kTileRows, Cfg::kMmaN);
       int g = 0, it = 0;
-      for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
+      for (int t = t_first; t < n_tiles; t += t_step, ++it) {
         const int a = it % Cfg::kNumAcc, use = it / Cfg::kNumAcc;
         const uint32_t acc = tmem + (uint32_t)(a * Cfg::kAccCols);
         if (it >= Cfg::kNumAcc && !mbar_wait(&acc_empty[a], (use - 1) & 1)) { *abort_flag = 1; }
-        if (*abort_flag) { umma_commit(&acc_full[a]); break; }
+        if (*abort_flag) { commit_both(&acc_full[a]); break; }
         tc_fence_after();
         for (int kb = 0; kb < nkb; ++kb, ++g) {
           const int s = g % Cfg::kStages;
@@ -493,15 +531,26 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             for (int sub = 0; sub < Cfg::kNSub; ++sub) {
               const uint64_t bo = (uint64_t)((sub * Cfg::kBoxRows * Cfg::kBK * 2) >> 4);
               const uint32_t d = acc + (uint32_t)(sub * Cfg::kMmaN);
-              umma_bf16(d, dAh + adv, dWh + bo + adv, idesc, (kb | kk) != 0);
-              umma_bf16(d, dAh + adv, dWl + bo + adv, idesc, 1u);
-              umma_bf16(d, dAl + adv, dWh + bo + adv, idesc, 1u);
+              if constexpr (PAIR) {
+                umma_bf16_pair(d, dAh + adv, dWh + bo + adv, idesc, (kb | kk) != 0);
+                umma_bf16_pair(d, dAh + adv, dWl + bo + adv, idesc, 1u);
+                umma_bf16_pair(d, dAl + adv, dWh + bo + adv, idesc, 1u);
+              } else {
+                umma_bf16(d, dAh + adv, dWh + bo + adv, idesc, (kb | kk) != 0);
+                umma_bf16(d, dAh + adv, dWl + bo + adv, idesc, 1u);
+                umma_bf16(d, dAl + adv, dWh + bo + adv, idesc, 1u);
+              }
             }
           }
-          umma_commit(&empty[s]);
+          commit_both(&empty[s]);
         }
-        umma_commit(&acc_full[a]);
+        commit_both(&acc_full[a]);
         if (*abort_flag) break;
+      }
+      if constexpr (PAIR) {
+        // both CTAs' epilogues have released the last accumulators
+        for (int j = it > Cfg::kNumAcc ? it - Cfg::kNumAcc : 0; j < it; ++j)
+          if (!mbar_wait(&acc_empty[j % Cfg::kNumAcc], (j / Cfg::kNumAcc) & 1)) break;
       }
     }
   } else {
@@ -520,9 +569,9 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     // column range of this part in whole 16-column chunks
     constexpr int kChunks = BN / 16;
     int it = 0;
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
+    for (int t = t_first; t < n_tiles; t += t_step, ++it) {
       const int a = it % Cfg::kNumAcc, use = it / Cfg::kNumAcc;
-      const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
+      const int m0 = (t / n_tiles_n) * Cfg::kTileRows + row_off, n0 = (t % n_tiles_n) * BN;
       const int c0 = (kChunks * part) / 4 * 16;
       const int c1 = (kChunks * (part + 1)) / 4 * 16;
       // RES_LN: this thread's residual row for the first kPre chunks, loaded
@@ -679,14 +728,19 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       // accumulator a may be overwritten once every epilogue warp has read it
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[a]);
+      if (lane == 0) {
+        if constexpr (PAIR) mbar_arrive_cluster(cluster_addr(&acc_empty[a], 0));
+        else mbar_arrive(&acc_empty[a]);
+      }
     }
   }
   if (MODE == EPI_F32 && warp >= 2 && lane == 0) bulk_wait_all();  // staging tiles stay valid until read
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();  // neither CTA leaves while the other may still signal it
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, Cfg::kTmemCols);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem, Cfg::kTmemCols);
+    else tmem_dealloc(tmem, Cfg::kTmemCols);
   }
 }
 
@@ -741,9 +795,43 @@ static bool make_out_map_f32(CUtensorMap* map, void* base, int cols, int rows, i
 
 static int g_num_sms[64] = {0};
 
+// CTA pairs (cta_group::2, 256-row tiles, each CTA staging half of W) for the
+// F32 epilogue at compress-tile sizes: in_proj (N = 4d, K = d) runs 8 %
+// faster at M = 262144 when each SM streams half the weight bytes.  Decode
+// steps (M = one row per chunk) stay on single CTAs, where the pair's start-up
+// costs more than it saves.  Both forms issue the same MMA sequence per row
+// and give bit-identical outputs, so the choice may depend on M.
+static constexpr bool pair_ok(int BN, int MODE) { return (BN == 128 || BN == 256) && MODE == EPI_F32; }
+static bool use_pair(int mode, int M) { return mode == EPI_F32 && M >= 65536; }
+
+template <int BN, int MODE>
+static cudaError_t launch_pair_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to,
+                                 const GemmArgs& a, cudaStream_t st) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int tiles = (a.N / BN) * ((a.M + 2 * kBM - 1) / (2 * kBM));
+  const int pairs = std::min(tiles, (g_num_sms[dev & 63] > 0 ? g_num_sms[dev & 63] : 148) / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kPThreads);
+  cfg.dynamicSmemBytes = PCfg<BN, true>::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_persist_kernel<BN, MODE, true>, ta, tw, to, a);
+}
+
 template <int BN, int MODE>
 static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const GemmArgs& a,
                             cudaStream_t st) {
+  if constexpr (pair_ok(BN, MODE)) {
+    if (use_pair(MODE, a.M)) return launch_pair_t<BN, MODE>(ta, tw, to, a, st);
+  }
   if constexpr (MODE <= EPI_RES_LN) {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -760,6 +848,11 @@ static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tw, const 
 
 template <int BN, int MODE>
 static cudaError_t set_attr_t() {
+  if constexpr (pair_ok(BN, MODE)) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_persist_kernel<BN, MODE, true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<BN, true>::kSmem);
+    if (e != cudaSuccess) return e;
+  }
   if constexpr (MODE <= EPI_RES_LN)
     return cudaFuncSetAttribute(gemm_persist_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 PCfg<BN>::kSmem);
@@ -837,7 +930,9 @@ cudaError_t gemm_launch(int mode, const __nv_bfloat16* A, long long a_plane, int
   CUtensorMap ta, tw, to;
   std::memset(&to, 0, sizeof(to));
   if (!make_plane_map(&ta, A, args.K, args.M, a_plane, kBM, box_k)) return cudaErrorInvalidValue;
-  if (!make_plane_map(&tw, W, args.K, args.N, w_plane, BN > 256 ? 256 : BN, box_k)) return cudaErrorInvalidValue;
+  const bool pair = use_pair(mode, args.M) && (BN == 128 || BN == 256) && mode <= EPI_RES_LN;
+  if (!make_plane_map(&tw, W, args.K, args.N, w_plane, pair ? BN / 2 : BN > 256 ? 256 : BN, box_k))
+    return cudaErrorInvalidValue;
   if (mode == EPI_F32 && !make_out_map_f32(&to, args.out_f32, args.N, args.M, args.ld_f32)) return cudaErrorInvalidValue;
   switch (BN) {
     case 48: return dispatch<48>(mode, ta, tw, to, args, stream);

@@ -176,6 +176,27 @@ def test_tile_size_does_not_change_the_stream(boa, m64):
         assert all(np.array_equal(a, b) for a, b in zip(outs[0], o))
 
 
+def test_cta_pair_gemm_bit_identical(boa, m256):
+    """Compress-sized GEMMs (M >= 65536 rows) run in_proj as CTA pairs
+    (cta_group::2); smaller ones on single CTAs.  The logits of 1100 x 64
+    positions in one call (M = 70400, pairs) equal those of the same rows in
+    two calls (M = 35200 each, single CTAs) bit for bit, and a compress batch
+    of 2048 chunks (M = 131072) writes the same streams as batches of 256."""
+    rng = np.random.default_rng(31)
+    tok = rng.integers(0, 256, (1100, 64), dtype=np.uint8)
+    whole = m256.logits(tok, 0)
+    halves = np.concatenate([m256.logits(tok[:550], 0), m256.logits(tok[550:], 0)])
+    assert np.array_equal(whole.view(np.uint32), halves.view(np.uint32))
+    data = boa.synth.particle_stream(2048 * 65, 32)
+    m256.set_batch(2048, 64)
+    big = m256.compress(data, 65)
+    m256.set_batch(256, 64)
+    small = m256.compress(data, 65)
+    m256.set_batch(0, 0)
+    assert all(np.array_equal(a, b) for a, b in zip(big, small))
+    assert m256.decompress(big[0], big[1], big[2], [65] * 2048, 65) == data
+
+
 def test_temperature_roundtrip(boa, m64):
     data = bytes(np.random.default_rng(10).integers(0, 256, 1500, dtype=np.uint8))
     m64.set_temperature(0.5)
