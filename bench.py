@@ -558,12 +558,12 @@ def main():
                                     "one batch"),
                        "d_model": a.d_model, "n_layers": a.layers, "chunks_per_gpu": C, "chunk_len": S,
                        "batch_chunks": C, "compress_tile": T, "parallelism": f"chunk-sharded x{ws}",
-                       "l2": (f"inputs ({n / MiB:g} MiB) and recurrent state "
-                              f"({C * a.layers * 19 * 2 * a.d_model * 4 / MiB / 1024:.2f} GiB) "
-                              + ("exceed L2 (126 MB); no flush needed" if n > 126e6 else
-                                 "state exceeds L2 (126 MB), inputs do not; no flush"
+                       "l2": (f"inputs {n / MiB:g} MiB, recurrent state "
+                              f"{C * a.layers * 19 * 2 * a.d_model * 4 / MiB / 1024:.2f} GiB: "
+                              + ("both exceed L2 (126 MB); no flush needed" if n > 126e6 else
+                                 "the state exceeds L2 (126 MB), the inputs do not; no flush"
                                  if C * a.layers * 19 * 2 * a.d_model * 4 > 126e6 else
-                                 "fit in L2 (126 MB): warm-cache timing, not a headline number")),
+                                 "both fit in L2 (126 MB): warm-cache timing, not a headline number")),
                        "warmup": f"{a.warmup} round trips of the same chunks truncated to {wl} B"},
             "compress_MBps": total / MiB / (comp_ms * 1e-3),
             "decompress_MBps": total / MiB / (dec_ms * 1e-3),
