@@ -77,6 +77,7 @@ SIGNATURES = {
     "boa_decompress_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64,
                                         C.c_uint32, C.c_uint32, C.c_void_p]),
     "boa_sync": (C.c_int, [C.c_void_p]),
+    "boa_selftest_wait_timeout": (C.c_int, [C.c_int, C.c_uint32]),
     "boa_device_bytes": (C.c_uint64, [C.c_void_p]),
     "boa_set_profiling": (C.c_int, [C.c_void_p, C.c_int]),
     "boa_profile_read": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_double), _u64p]),

@@ -40,6 +40,8 @@ cudaError_t launch_scan(const float* delta, int ld_delta, int r, const float* dt
                         float* ssm_state, __nv_bfloat16* yhl, long long plane, int B, int T, cudaStream_t st);
 
 cudaError_t scan_prepare_device();
+// one bounded mbarrier wait that runs out (failure-detection self-test)
+cudaError_t launch_wait_selftest(uint64_t limit_ns, int* ok);
 
 // minGRU recurrence: h = (1-z) h + z g(ht) over T rows per chunk; writes h
 // into x_out rows (boa_gpu.hpp:652-693).  zh = [M][2d] (z logits | h~ raw).

@@ -677,6 +677,20 @@ cudaError_t launch_rc_decode_init(DecState* ds, const uint32_t* payload, const u
   return cudaGetLastError();
 }
 
+// Failure-detection self-test: one thread waits on a shared-memory barrier
+// that nothing arrives on.  The bounded wait gives up after limit_ns, records
+// BOA_ERR_TIMEOUT in the device error word and the kernel returns normally.
+__global__ void wait_selftest_kernel(uint64_t limit_ns, int* ok) {
+  __shared__ uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  *ok = mbar_wait_for(&bar, 0, limit_ns) ? 1 : 0;
+}
+cudaError_t launch_wait_selftest(uint64_t limit_ns, int* ok) {
+  wait_selftest_kernel<<<1, 1>>>(limit_ns, ok);
+  return cudaGetLastError();
+}
+
 __global__ void set_counter_kernel(int* d_t, int v) { *d_t = v; }
 __global__ void increment_kernel(int* d_t) { *d_t += 1; }
 cudaError_t launch_set_counter(int* d_t, int v, cudaStream_t st) {

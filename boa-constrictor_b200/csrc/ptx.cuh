@@ -58,18 +58,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Bounded wait for the phase with the given parity to complete: past the
+// limit it records BOA_ERR_TIMEOUT in the device error word and returns false,
+// and the caller unwinds without touching the barrier's data.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = global_ns();
   while (true) {
     if (mbar_try_wait(a, parity)) return true;
-    if (global_ns() - t0 > kWaitLimitNs) {
+    if (global_ns() - t0 > limit_ns) {
       set_dev_error(BOA_ERR_TIMEOUT);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  return mbar_wait_for(bar, parity, kWaitLimitNs);
 }
 
 // named barrier over a subset of warps (ids 1..15; id 0 is __syncthreads)

@@ -734,6 +734,28 @@ uint64_t boa_device_bytes(const boa_model* m) {
   return m ? (uint64_t)(m->wbytes + m->work_bytes + m->io_bytes) : 0;
 }
 
+int boa_selftest_wait_timeout(int device, uint32_t limit_us) {
+  int n_dev = 0;
+  if (cudaGetDeviceCount(&n_dev) != cudaSuccess || device < 0 || device >= n_dev) {
+    cudaGetLastError();
+    return fail(nullptr, BOA_E_INVALID, "no such CUDA device");
+  }
+  if (limit_us == 0 || limit_us > 1000000u) return fail(nullptr, BOA_E_INVALID, "limit_us must be in [1, 1e6]");
+  DeviceGuard dev(device);
+  int code = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&code, boa::g_dev_error, sizeof(int));
+  if (e == cudaSuccess && code != 0) return fail(nullptr, BOA_E_DEVICE, "device error word was already set");
+  int* d_ok = nullptr;
+  if ((e = cudaMalloc(&d_ok, sizeof(int))) != cudaSuccess) return cuda_fail(nullptr, e, "self-test allocation");
+  e = boa::launch_wait_selftest((uint64_t)limit_us * 1000ull, d_ok);
+  int ok = -1;
+  if (e == cudaSuccess) e = cudaMemcpy(&ok, d_ok, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(d_ok);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "self-test launch");
+  if (int rc = read_dev_error(nullptr)) return rc;  // expected: the wait ran out
+  return fail(nullptr, BOA_E_CUDA, ok ? "self-test barrier completed without an arrival" : "no error recorded");
+}
+
 int boa_sync(boa_model* m) {
   if (!m) return BOA_E_INVALID;
   DeviceGuard dev(m->device);

@@ -113,6 +113,15 @@ int boa_decompress_device(boa_model* h, const uint32_t* d_payload, const uint64_
  * which this call reads and clears: with several handles on one device, a
  * failure is reported to whichever handle synchronises first. */
 int boa_sync(boa_model* h);
+/* Failure-detection self-test (no counterpart in the reference): one kernel
+ * on `device` waits on a barrier that nothing signals, with the bounded wait
+ * every kernel of this library uses, cut to limit_us microseconds (1 .. 1e6).
+ * The wait gives up, records the timeout in the device's error word and the
+ * kernel returns, so the context stays usable.  Returns BOA_E_DEVICE with
+ * boa_last_error(NULL) = "device wait timed out" when that happened (the
+ * expected outcome; the error word is cleared), BOA_E_INVALID for a bad
+ * device or limit, BOA_E_CUDA otherwise. */
+int boa_selftest_wait_timeout(int device, uint32_t limit_us);
 /* Device memory the handle holds (weights + work buffers + states). */
 uint64_t boa_device_bytes(const boa_model* h);
 

@@ -64,6 +64,15 @@ def test_null_handle_is_rejected(boa):
     assert L.boa_device_bytes(None) == 0
 
 
+def test_wait_selftest_rejects_bad_arguments(boa):
+    """No kernel runs for an absent device or a limit outside [1 us, 1 s]."""
+    L = boa.lib()
+    assert L.boa_selftest_wait_timeout(-1, 1000) == boa.BOA_E_INVALID
+    assert L.boa_selftest_wait_timeout(4096, 1000) == boa.BOA_E_INVALID
+    assert L.boa_selftest_wait_timeout(0, 0) in (boa.BOA_E_INVALID,)
+    assert L.boa_selftest_wait_timeout(0, 2_000_000) == boa.BOA_E_INVALID
+
+
 def _streams(rng, n, chunk):
     sizes = rng.integers(0, chunk // 4, n).astype(np.uint32)
     sizes[-1] = 0

@@ -197,6 +197,40 @@ def test_cta_pair_gemm_bit_identical(boa, m256):
     assert m256.decompress(big[0], big[1], big[2], [65] * 2048, 65) == data
 
 
+def test_device_wait_timeout_is_reported_and_context_survives(boa, m64):
+    """Failure detection without a GPU fault: a kernel waits on a barrier that
+    nothing signals, its bounded wait (cut to 20 ms) gives up and records the
+    timeout, the host reads it as BOA_E_DEVICE, the error word is cleared, and
+    the same context then runs a byte-exact round trip."""
+    import time
+    L = boa.lib()
+    t0 = time.monotonic()
+    assert L.boa_selftest_wait_timeout(0, 20000) == boa.BOA_E_DEVICE
+    assert time.monotonic() - t0 < 10
+    assert b"timed out" in L.boa_last_error(None)
+    m64.sync()
+    data = bytes(np.random.default_rng(12).integers(0, 256, 900, dtype=np.uint8))
+    fb, sizes, pay = m64.compress(data, 300)
+    assert m64.decompress(fb, sizes, pay, [300] * 3, 300) == data
+    m64.sync()
+
+
+def test_cli_reports_a_missing_gpu_shard(boa, weights, tmp_path):
+    """A shard whose GPU does not exist fails its own host thread; the CLI
+    reports it, exits non-zero and writes no container."""
+    import torch
+    n = torch.cuda.device_count()
+    src = tmp_path / "in.bin"
+    src.write_bytes(boa.synth.particle_stream(4000, 3))
+    out = tmp_path / "out.boa"
+    cli = os.path.join(os.path.dirname(boa.__file__), "bin", "boa_constrictor")
+    r = subprocess.run([cli, "compress", weights("mamba", 64, 2, 3), str(src), str(out), "64", "2",
+                        "--chunk-size", "500", "--gpus", str(n + 1)], capture_output=True, text=True)
+    assert r.returncode != 0
+    assert "Error" in r.stderr
+    assert not out.exists()
+
+
 def test_temperature_roundtrip(boa, m64):
     data = bytes(np.random.default_rng(10).integers(0, 256, 1500, dtype=np.uint8))
     m64.set_temperature(0.5)

@@ -64,3 +64,49 @@ def test_shard_ranges_cover_exactly(boa):
             got = [boa.sharding.shard_range(n, r, world) for r in range(world)]
             assert sum(k for _, k in got) == n
             assert all(got[r][0] + got[r][1] == got[r + 1][0] for r in range(world - 1))
+
+
+def _worker_failing(rank, world, port, mode, out_dir):
+    """Rank 1 fails: with mode "error" it reports a coder failure through the
+    gather, with mode "leave" it exits without joining it.  Every rank writes
+    what it saw to out_dir/rank<r>.txt."""
+    import datetime
+    boa = load_package()
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    if rank == 1 and mode == "leave":
+        os._exit(0)
+    fb = np.full(2, rank, np.uint8)
+    sizes = np.array([1, 1], np.uint32)
+    pay = np.array([rank, rank + 1], np.uint32)
+    err = "simulated coder failure" if (rank == 1 and mode == "error") else None
+    try:
+        boa.sharding.gather_container(2 * world * 10, 10, fb, sizes, pay, dist=dist, error=err)
+        seen = "ok"
+    except boa.sharding.ShardError as e:
+        seen = f"ShardError: {e}"
+    with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
+        f.write(seen)
+    if mode == "error":
+        dist.destroy_process_group()
+    else:
+        os._exit(0)  # the group lost a member; leave without a collective teardown
+
+
+@pytest.mark.parametrize("mode", ["error", "leave"])
+def test_failed_rank_is_reported_not_waited_for(boa, tmp_path, mode):
+    """Failure detection on the host: a rank that reports an error, or that
+    leaves the job, makes the gather raise ShardError on the ranks still
+    running (naming the failed rank when it reported), instead of leaving
+    them blocked in the collective."""
+    import time
+    t0 = time.monotonic()
+    mp.spawn(_worker_failing, args=(2, _free_port(), mode, str(tmp_path)), nprocs=2, join=True)
+    assert time.monotonic() - t0 < 60
+    r0 = (tmp_path / "rank0.txt").read_text()
+    assert r0.startswith("ShardError")
+    if mode == "error":
+        assert "rank 1 failed: simulated coder failure" in r0
+        assert (tmp_path / "rank1.txt").read_text().startswith("ShardError")
+    else:
+        assert not (tmp_path / "rank1.txt").exists()
