@@ -715,6 +715,9 @@ __global__ void rc_encode_cdf_kernel(EncState* es, const uint32_t* __restrict__ 
     const int sym = syms[rowi];
     const uint32_t* q = cdf + rowi * 257;
     const uint32_t lo = q[sym], hi = q[sym + 1];
+    // a caller-supplied CDF must give the coded symbol a non-empty interval
+    // inside [0, 2^24]; anything else would code a stream that cannot decode
+    if (hi <= lo || hi > (1u << 24)) { set_dev_error(BOA_ERR_BAD_INPUT); break; }
     if (!enc_symbol(s, lo, hi - lo, out, pitch)) { set_dev_error(BOA_ERR_STREAM_OVERFLOW); break; }
   }
   es[i] = s;

@@ -439,7 +439,9 @@ int read_dev_error(boa_model* m) {
     cudaMemcpyToSymbol(boa::g_dev_error, &zero, sizeof(int));
     return fail(m, BOA_E_DEVICE, code == boa::BOA_ERR_TIMEOUT ? "device wait timed out"
                                  : code == boa::BOA_ERR_STREAM_OVERFLOW ? "range-coded stream exceeded its capacity"
-                                                                        : "device-side check failed");
+                                 : code == boa::BOA_ERR_BAD_INPUT
+                                     ? "a CDF gives a coded symbol an empty interval or one above 2^24"
+                                     : "device-side check failed");
   }
   return 0;
 }

@@ -149,6 +149,9 @@ int boa_model_logits(boa_model* h, const uint8_t* tokens, int B, int L, int mode
 /* ---- range coder on explicit integer CDFs --------------------------------
  * CDFs Q[n_steps][n_streams][257] (Q[s] = cumulative frequency of symbols
  * below s, Q[256] = 2^24, strictly increasing), symbols [n_steps][n_streams].
+ * The encoder checks the interval of every coded symbol (Q[s] < Q[s+1] <=
+ * 2^24) and returns BOA_E_DEVICE for one that is empty or out of range,
+ * where the reference would silently write an undecodable stream.
  * Replaces the coder of ker_rc_encode_chunk_parallel_warp / ker_rc_finish /
  * ker_rc_init_decoder / ker_rc_decode_fused_step_warp
  * (range_coder_kernels.cu:46-60, :279-335, :725-780, :916-968) for callers
@@ -171,7 +174,9 @@ int boa_rc_decode_cdf(boa_model* h, const uint32_t* cdf, int n_streams, int n_st
  * synchronised.  The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress), so make it before any stream capture.
  * Every call shares the array and resets the states it uses: calls that
- * overlap on the GPU race.  Errors are reported by boa_last_error(NULL). */
+ * overlap on the GPU race.  Errors are reported by boa_last_error(NULL);
+ * the device-side checks (stream capacity, empty CDF interval) land in the
+ * device's error word, read and cleared by the next boa_sync() on it. */
 int boa_rc_encode_cdf_noalloc(const uint32_t* d_cdf, const uint8_t* d_syms, int n_streams, int n_steps,
                               uint32_t* d_words, uint32_t pitch_words, uint32_t* d_sizes, void* stream);
 /* The integer CDF the library derives from one or more logits rows

@@ -56,6 +56,28 @@ def test_rc_configs1_geometry_bit_exact(boa, oracle, m64, n_streams, n_steps):
     assert np.array_equal(m64.rc_decode_cdf(Q, sizes, pay), syms)
 
 
+def test_rc_encode_rejects_an_empty_interval(boa, m64):
+    """A caller CDF that gives a coded symbol zero frequency (or a top above
+    2^24) is reported as BOA_E_DEVICE instead of coding an undecodable stream;
+    the handle keeps working."""
+    rng = np.random.default_rng(77)
+    Q, syms = dirichlet_cdfs(rng, 50, 3)
+    bad = Q.copy()
+    s0 = int(syms[10, 1])
+    bad[10, 1, s0 + 1] = bad[10, 1, s0]  # empty interval for the coded symbol
+    with pytest.raises(boa.BoaError) as e:
+        m64.rc_encode_cdf(bad, syms)
+    assert e.value.code == boa.BOA_E_DEVICE and "empty interval" in str(e.value)
+    top = Q.copy()
+    top[0, 0, 256] = (1 << 24) + 1
+    top_syms = syms.copy()
+    top_syms[0, 0] = 255
+    with pytest.raises(boa.BoaError):
+        m64.rc_encode_cdf(top, top_syms)
+    sizes, pay = m64.rc_encode_cdf(Q, syms)
+    assert np.array_equal(m64.rc_decode_cdf(Q, sizes, pay), syms)
+
+
 def test_rc_frequency_one_symbols(boa, oracle, m64):
     n = 500
     Q = np.zeros((n, 2, 257), np.uint32)
