@@ -206,6 +206,13 @@ def cpu_sample(weights, d, L, chunk_len, seed, budget_s, threads):
     return len(sub) / MiB / dt, f"{threads} chunks x {plen}-byte prefixes of configs[2] chunks, round trip", dt
 
 
+def workload_name(a, C, S):
+    """The workload string both arms report for this geometry."""
+    n = C * S
+    tag = "configs[2]: " if (a.d_model, a.layers, C, S) == (256, 8, 16384, 16384) else ""
+    return f"{tag}mamba d{a.d_model} L{a.layers}, {C} chunks x {S} B = {n / MiB:g} MiB per GPU, one batch"
+
+
 def run_reference(a):
     ws, rank, _ = dist_info()
     if rank != 0:
@@ -218,16 +225,19 @@ def run_reference(a):
         boa.synth.write_random_weights(w, "mamba", a.d_model, a.layers, 0)
         for _ in range(a.warmup):
             cpu_sample(w, a.d_model, a.layers, a.chunk_len, 1, 0.2, threads)
-        vals = []
+        vals, secs = [], []
         for _ in range(a.steps):
-            v, sample, _ = cpu_sample(w, a.d_model, a.layers, a.chunk_len, 1, a.cpu_seconds, threads)
+            v, sample, dt = cpu_sample(w, a.d_model, a.layers, a.chunk_len, 1, a.cpu_seconds, threads)
             vals.append(v)
+            secs.append(dt)
     v = statistics.median(vals)
     line = {"metric": "compress+decompress round-trip MB/s", "value": v, "unit": "MB/s", "n_gpus": ws,
-            "steps": a.steps, "warmup": a.warmup, "ms_per_step": None, "higher_is_better": True,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": statistics.median(secs) * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": f"configs[2] mamba d{a.d_model} L{a.layers}, chunk {a.chunk_len} B, CPU sample"},
+            "config": {"workload": workload_name(a, a.chunks, a.chunk_len),
+                       "step": "a bounded sample of the workload per step (cpu_baseline.sample); ms_per_step is its "
+                               "duration"},
             "cpu_baseline": {"value": v, "unit": "MB/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": "MB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -553,9 +563,7 @@ def main():
             "unit": "MB/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup, "ms_per_step": step_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16x3 (fp32-accurate)",
             "data": "synthetic: seeded float32 particle records, random-init weights",
-            "config": {"workload": (f"{'configs[2]: ' if (a.d_model, a.layers, C, S) == (256, 8, 16384, 16384) else ''}"
-                                    f"mamba d{a.d_model} L{a.layers}, {C} chunks x {S} B = {n / MiB:g} MiB per GPU, "
-                                    "one batch"),
+            "config": {"workload": workload_name(a, C, S),
                        "d_model": a.d_model, "n_layers": a.layers, "chunks_per_gpu": C, "chunk_len": S,
                        "batch_chunks": C, "compress_tile": T, "parallelism": f"chunk-sharded x{ws}",
                        "l2": (f"inputs {n / MiB:g} MiB, recurrent state "
