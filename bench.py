@@ -87,8 +87,8 @@ def algorithmic_per_launch(cls, B, T, d, L):
     xp = ((d + 15) // 16 + 32 + 15) // 16 * 16
     gem = {"in_proj": (d, 4 * d), "x_proj": (di, xp), "out_proj_ln": (di, d), "ff2_res_ln": (4 * d, d),
            "head1": (d, d), "head2_coder": (d, 256)}
-    if cls == "ffn":  # fused feed-forward (both GEMMs) for d <= 256, its first GEMM otherwise
-        return "tensor", 2.0 * 3 * M * (4 * d * d) * (2 if d <= 256 else 1)
+    if cls == "ffn":  # fused feed-forward (both GEMMs) for d 64 / 128 / 256, its first GEMM otherwise
+        return "tensor", 2.0 * 3 * M * (4 * d * d) * (2 if d in (64, 128, 256) else 1)
     if cls in gem:
         K, N = gem[cls]
         return "tensor", 2.0 * 3 * M * N * K

@@ -901,7 +901,9 @@ cudaError_t gemm_prepare_device() {
   if ((e = cudaDeviceGetAttribute(&g_num_sms[dev & 63], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
   if ((e = set_attrs<48>()) != cudaSuccess) return e;
   if ((e = set_attrs<64>()) != cudaSuccess) return e;
+  if ((e = set_attrs<80>()) != cudaSuccess) return e;   // d_model 80: LayerNorm rows, head1
   if ((e = set_attrs<128>()) != cudaSuccess) return e;
+  if ((e = set_attrs<160>()) != cudaSuccess) return e;  // d_model 160
   if ((e = set_attrs<256>()) != cudaSuccess) return e;
   if ((e = set_attr_t<512, EPI_LN_SPLIT>()) != cudaSuccess) return e;
   return set_attr_t<512, EPI_RES_LN>();
@@ -923,7 +925,8 @@ cudaError_t gemm_launch(int mode, const __nv_bfloat16* A, long long a_plane, int
   if (args.K % 16 != 0 || args.K <= 0 || args.M <= 0) return cudaErrorInvalidValue;
   if (mode <= EPI_RES_LN && args.N > kMaxPersistN) return cudaErrorInvalidValue;  // bias staging size
   const int BN = pick_bn(mode, args.N);
-  if (BN != 48 && BN != 64 && BN != 128 && BN != 256 && BN != 512) return cudaErrorInvalidValue;
+  if (BN != 48 && BN != 64 && BN != 80 && BN != 128 && BN != 160 && BN != 256 && BN != 512)
+    return cudaErrorInvalidValue;
   if (mode >= EPI_LOGITS && BN != 256) return cudaErrorInvalidValue;
   // persistent row-parallel modes with BN >= 128 use K-blocks of 32
   const int box_k = (mode <= EPI_RES_LN && BN >= 128) ? 32 : kBK;
@@ -937,7 +940,9 @@ cudaError_t gemm_launch(int mode, const __nv_bfloat16* A, long long a_plane, int
   switch (BN) {
     case 48: return dispatch<48>(mode, ta, tw, to, args, stream);
     case 64: return dispatch<64>(mode, ta, tw, to, args, stream);
+    case 80: return dispatch<80>(mode, ta, tw, to, args, stream);
     case 128: return dispatch<128>(mode, ta, tw, to, args, stream);
+    case 160: return dispatch<160>(mode, ta, tw, to, args, stream);
     case 512:
       if (mode == EPI_LN_SPLIT) return launch_t<512, EPI_LN_SPLIT>(ta, tw, to, args, stream);
       if (mode == EPI_RES_LN) return launch_t<512, EPI_RES_LN>(ta, tw, to, args, stream);

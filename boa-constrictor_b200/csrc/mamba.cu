@@ -22,13 +22,14 @@ __device__ __forceinline__ int chunk_len_of(long long n_bytes, int chunk_len, in
 }
 
 // ---------------------------------------------------------------- embedding + LN
-// One warp per row, D/32 values per lane.  Restates the embedding gather
+// One warp per row, ceil(D/32) values per lane (the last ones guarded when
+// D is not a multiple of 32, as d_model 80).  Restates the embedding gather
 // (utility_kernels.cu:46-72) and LN1 (inference_kernels.cu:293-348).
 template <int D>
 __global__ void embed_ln_kernel(TokenSrc src, const float* __restrict__ emb, float* __restrict__ x,
                                 __nv_bfloat16* __restrict__ xn, long long plane, const float* __restrict__ w,
                                 const float* __restrict__ bb, int M) {
-  constexpr int V = D / 32;
+  constexpr int V = (D + 31) / 32;
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
@@ -49,8 +50,11 @@ __global__ void embed_ln_kernel(TokenSrc src, const float* __restrict__ emb, flo
   float s = 0.f, sq = 0.f;
 #pragma unroll
   for (int i = 0; i < V; ++i) {
-    v[i] = emb[(size_t)tok * D + lane + 32 * i];
-    x[(size_t)row * D + lane + 32 * i] = v[i];
+    v[i] = 0.f;
+    if (lane + 32 * i < D) {
+      v[i] = emb[(size_t)tok * D + lane + 32 * i];
+      x[(size_t)row * D + lane + 32 * i] = v[i];
+    }
     s += v[i];
     sq += v[i] * v[i];
   }
@@ -62,6 +66,7 @@ __global__ void embed_ln_kernel(TokenSrc src, const float* __restrict__ emb, flo
 #pragma unroll
   for (int i = 0; i < V; ++i) {
     const int c = lane + 32 * i;
+    if (c >= D) break;
     const float y = (v[i] - mean) * inv_std * w[c] + bb[c];
     __nv_bfloat16 h, l;
     split_bf16(y, h, l);
@@ -76,7 +81,9 @@ cudaError_t launch_embed_ln(const TokenSrc& src, const float* emb, int d, float*
   dim3 grid((M + rows_per_block - 1) / rows_per_block), block(32 * rows_per_block);
   switch (d) {
     case 64: embed_ln_kernel<64><<<grid, block, 0, st>>>(src, emb, x, xn, plane, w, b, M); break;
+    case 80: embed_ln_kernel<80><<<grid, block, 0, st>>>(src, emb, x, xn, plane, w, b, M); break;
     case 128: embed_ln_kernel<128><<<grid, block, 0, st>>>(src, emb, x, xn, plane, w, b, M); break;
+    case 160: embed_ln_kernel<160><<<grid, block, 0, st>>>(src, emb, x, xn, plane, w, b, M); break;
     case 256: embed_ln_kernel<256><<<grid, block, 0, st>>>(src, emb, x, xn, plane, w, b, M); break;
     case 512: embed_ln_kernel<512><<<grid, block, 0, st>>>(src, emb, x, xn, plane, w, b, M); break;
     default: return cudaErrorInvalidValue;
@@ -454,7 +461,7 @@ cudaError_t launch_mingru(const float* zh, int d, float* hs, float* xo, int B, i
 template <int D, bool RMS>
 __global__ void add_ln_kernel(float* __restrict__ x, const float* __restrict__ y, __nv_bfloat16* __restrict__ xn,
                               long long plane, const float* __restrict__ w, const float* __restrict__ bb, int M) {
-  constexpr int V = D / 32;
+  constexpr int V = (D + 31) / 32;  // the last ones guarded when D is not a multiple of 32
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
@@ -462,6 +469,8 @@ __global__ void add_ln_kernel(float* __restrict__ x, const float* __restrict__ y
   float s = 0.f, sq = 0.f;
 #pragma unroll
   for (int i = 0; i < V; ++i) {
+    v[i] = 0.f;
+    if (lane + 32 * i >= D) continue;
     const size_t o = (size_t)row * D + lane + 32 * i;
     float t = x[o];
     if (y) { t = y[o] + t; x[o] = t; }
@@ -479,6 +488,7 @@ __global__ void add_ln_kernel(float* __restrict__ x, const float* __restrict__ y
 #pragma unroll
   for (int i = 0; i < V; ++i) {
     const int c = lane + 32 * i;
+    if (c >= D) break;
     const float o = RMS ? v[i] * inv * w[c] : (v[i] - mean) * inv * w[c] + bb[c];
     __nv_bfloat16 h, l;
     split_bf16(o, h, l);
@@ -492,7 +502,9 @@ static cudaError_t launch_add_ln_t(float* x, const float* y, int d, __nv_bfloat1
   dim3 grid((M + 7) / 8), block(256);
   switch (d) {
     case 64: add_ln_kernel<64, RMS><<<grid, block, 0, st>>>(x, y, xn, plane, w, b, M); break;
+    case 80: add_ln_kernel<80, RMS><<<grid, block, 0, st>>>(x, y, xn, plane, w, b, M); break;
     case 128: add_ln_kernel<128, RMS><<<grid, block, 0, st>>>(x, y, xn, plane, w, b, M); break;
+    case 160: add_ln_kernel<160, RMS><<<grid, block, 0, st>>>(x, y, xn, plane, w, b, M); break;
     case 256: add_ln_kernel<256, RMS><<<grid, block, 0, st>>>(x, y, xn, plane, w, b, M); break;
     case 512: add_ln_kernel<512, RMS><<<grid, block, 0, st>>>(x, y, xn, plane, w, b, M); break;
     default: return cudaErrorInvalidValue;

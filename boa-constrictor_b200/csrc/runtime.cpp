@@ -215,7 +215,7 @@ enum ProfClass {
   PC_EMBED = 0, PC_IN_PROJ, PC_CONV, PC_X_PROJ, PC_SCAN, PC_OUT_PROJ_LN, PC_FF1, PC_FF2_LN, PC_HEAD1, PC_HEAD2_CODER,
   PC_ENCODE, PC_OTHER
 };
-// "ffn": the fused feed-forward kernel (d <= 256), or its first GEMM (d = 512)
+// "ffn": the fused feed-forward kernel (d 64, 128, 256), or its first GEMM (other widths)
 const char* const kProfNames[BOA_PROF_CLASSES] = {"embed_ln", "in_proj", "conv", "x_proj", "scan", "out_proj_ln",
                                                   "ffn", "ff2_res_ln", "head1", "head2_coder", "encode_tile",
                                                   "other"};
@@ -403,7 +403,7 @@ int forward(boa_model* m, const boa::TokenSrc& src, int B, int T, int head_mode,
       BOA_LAUNCH(PC_SCAN, boa::launch_mingru(m->xz, d, hst, m->u, B, T, st));
       BOA_LAUNCH(PC_OTHER, boa::launch_add_ln(m->x, m->u, d, m->xn, xn_plane, w.ln2w, w.ln2b, M, st));
     }
-    if (d <= 256) {  // fused feed-forward: the hidden activation stays on chip
+    if (d == 64 || d == 128 || d == 256) {  // fused feed-forward: the hidden activation stays on chip
       a = boa::GemmArgs{}; a.M = M;
       a.N = d; a.bias = w.ff2_b; a.res = m->x; a.out_hl = m->xn; a.ld_hl = d; a.plane_hl = xn_plane;
       if (!last) { a.ln_w = m->layers[l + 1].ln1w; a.ln_b = m->layers[l + 1].ln1b; }
@@ -543,8 +543,13 @@ int boa_model_load(const char* path, int backbone, int d, int nl, int device, bo
   *out = nullptr;
   if (backbone < BOA_BACKBONE_MAMBA || backbone > BOA_BACKBONE_MINGRU)
     return fail(nullptr, BOA_E_INVALID, "backbone must be mamba (0), lstm (1), gru (2) or mingru (3)");
-  if (!(d == 64 || d == 128 || d == 256 || d == 512) || nl <= 0 || nl > 256)
-    return fail(nullptr, BOA_E_INVALID, "d_model must be 64, 128, 256 or 512 and n_layers in 1..256");
+  // widths of the reference's checkpoints (mamba d 64 / 80 / 128, minGRU d 160 / 256) and the configs
+  const bool rnn = backbone == BOA_BACKBONE_LSTM || backbone == BOA_BACKBONE_GRU;
+  const bool d_ok = d == 64 || d == 128 || d == 256 || d == 512 || (!rnn && (d == 80 || d == 160));
+  if (!d_ok || nl <= 0 || nl > 256)
+    return fail(nullptr, BOA_E_INVALID,
+                "d_model must be 64, 80, 128, 160, 256 or 512 (LSTM / GRU: 64, 128, 256 or 512) and n_layers "
+                "in 1..256");
   FileReader R;
   {
     FILE* f = path ? std::fopen(path, "rb") : nullptr;
@@ -563,9 +568,14 @@ int boa_model_load(const char* path, int backbone, int d, int nl, int device, bo
     R.off = 4;
   }
   std::unique_ptr<boa_model> m(new boa_model());
-  m->device = device; m->backbone = backbone; m->d = d; m->L = nl; m->di = 2 * d; m->r = (d + 15) / 16;
+  m->device = device; m->backbone = backbone; m->d = d; m->L = nl; m->di = 2 * d;
+  // dt_rank = ceil(d / 16) in the file; the scan runs 4, 8, 16 or 32 dt inputs, so an odd rank (d 80: 5,
+  // d 160: 10) is zero-padded: x_proj gets zero rows after its dt rows and dt_proj zero columns, which
+  // add exact zeros to the dt dot product
+  const int r = (d + 15) / 16;
+  m->r = r <= 4 ? 4 : r <= 8 ? 8 : r <= 16 ? 16 : 32;
   m->xpN = ((m->r + 32 + 15) / 16) * 16;
-  const int di = m->di, r = m->r;
+  const int di = m->di, rp = m->r;
 
   // ---- parse in file order into host vectors (boa_gpu.hpp:990-1029)
   struct HostHL { std::vector<uint16_t> v; int N, K; };
@@ -597,8 +607,20 @@ int boa_model_load(const char* path, int backbone, int d, int nl, int device, bo
       x.in_b = addf(R.vec(2 * di));
       x.conv_w = addf(R.vec((size_t)di * 4));
       x.conv_b = addf(R.vec(di));
-      x.xp = addh(make_hl(R.vec((size_t)(r + 32) * di), r + 32, di, m->xpN));
-      x.dt_w = addf(R.vec((size_t)di * r));
+      {
+        // x_proj rows [dt (r) | B (16) | C (16)] -> [dt (r) | 0 (rp - r) | B | C]
+        const std::vector<float> xw = R.vec((size_t)(r + 32) * di);
+        std::vector<float> xp((size_t)(rp + 32) * di, 0.f);
+        std::copy(xw.begin(), xw.begin() + (size_t)r * di, xp.begin());
+        std::copy(xw.begin() + (size_t)r * di, xw.end(), xp.begin() + (size_t)rp * di);
+        x.xp = addh(make_hl(xp, rp + 32, di, m->xpN));
+        // dt_proj [di][r] -> [di][rp]
+        const std::vector<float> dw = R.vec((size_t)di * r);
+        std::vector<float> dtw((size_t)di * rp, 0.f);
+        for (int c = 0; c < di; ++c) std::copy(dw.begin() + (size_t)c * r, dw.begin() + (size_t)(c + 1) * r,
+                                               dtw.begin() + (size_t)c * rp);
+        x.dt_w = addf(std::move(dtw));
+      }
       x.dt_b = addf(R.vec(di));
       std::vector<float> alog = R.vec((size_t)di * 16);
       // stored as A * log2(e) with A = -exp(A_log): the scan evaluates exp(A dt) as 2^(na2 dt)

@@ -45,7 +45,11 @@ typedef struct boa_model boa_model;
  * convert_boa_weights.py:153-241 ("BOA\0" fp32 or "BOA\1" fp16 header, or a
  * headerless legacy fp32 file); d_model and n_layers are not stored in the
  * file and must be given, as on the reference CLI (boa.cpp:912-919).  The
- * file size must match the dims exactly (BOA_E_FORMAT otherwise). */
+ * file size must match the dims exactly (BOA_E_FORMAT otherwise).  d_model
+ * is one of 64, 80, 128, 160, 256, 512 (the widths of the reference's
+ * checkpoints and configs; LSTM / GRU: 64, 128, 256, 512).  An odd dt_rank
+ * (ceil(d_model / 16): 5 at 80, 10 at 160) is zero-padded to 8 / 16 on load:
+ * the padded terms add exact zeros to the dt projection. */
 int boa_model_load(const char* weights_path, int backbone, int d_model, int n_layers, int device,
                    boa_model** out);
 /* Every call on a handle runs on the handle's device and leaves the calling

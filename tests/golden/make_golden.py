@@ -21,6 +21,14 @@ manifest.json, so only reference OUTPUTS are stored):
                          under the configs[0] model: container layout and the
                          reference's bits/byte
   manifest.json          parameters, sizes, sha256, reference round-trip flags
+
+With --trained it writes only the trained-checkpoint fixtures (weights
+converted by convert_trained.py) and merges them into manifest.json:
+  ref_logits_trained_<name>.npz  tokens (bytes of the particle stream) and
+                                 the reference's logits in both forms
+  manifest "trained_result"      size, sha256 and round-trip flag of the
+                                 reference CLI's container of 64 KiB of
+                                 particle records under each model
 """
 import hashlib
 import importlib.util
@@ -55,6 +63,62 @@ RAND = dict(d_model=256, n_layers=8, seed=0, n_bytes=65536, data_seed=1, chunk=4
 PYRC = [dict(name="k256", seed=21, N=48, T=160, K=256, alpha=0.1),
         dict(name="k7", seed=22, N=33, T=90, K=7, alpha=0.5),
         dict(name="k1000", seed=23, N=9, T=40, K=1000, alpha=0.05)]
+
+
+# trained checkpoints (tests/golden/trained_<name>.bin, see convert_trained.py)
+TRAINED = [dict(name="mamba_d64L2", backbone="mamba", d_model=64, n_layers=2),
+           dict(name="mamba_d80L1", backbone="mamba", d_model=80, n_layers=1),
+           dict(name="mingru_d160L1", backbone="mingru", d_model=160, n_layers=1)]
+TRAINED_DATA = dict(n_bytes=65536, data_seed=41, chunk=4096, batch=16, B=3, T=64)
+
+
+def trained_tokens():
+    """B rows of T consecutive bytes of the particle stream (the models' own
+    kind of input), row b starting at byte b * chunk."""
+    data = np.frombuffer(synth.particle_stream(TRAINED_DATA["n_bytes"], TRAINED_DATA["data_seed"]), np.uint8)
+    B, T, S = TRAINED_DATA["B"], TRAINED_DATA["T"], TRAINED_DATA["chunk"]
+    return np.stack([data[b * S: b * S + T] for b in range(B)])
+
+
+def main_trained(out_dir):
+    tmp = os.path.join(out_dir, "_tmp")
+    os.makedirs(tmp, exist_ok=True)
+    man = json.load(open(os.path.join(out_dir, "manifest.json")))
+    man["trained"] = TRAINED
+    man["trained_data"] = TRAINED_DATA
+    man["trained_result"] = {}
+    tok = trained_tokens()
+    tf = os.path.join(tmp, "tok.u8")
+    tok.tofile(tf)
+    data = synth.particle_stream(TRAINED_DATA["n_bytes"], TRAINED_DATA["data_seed"])
+    fin = os.path.join(tmp, "trained.in"); open(fin, "wb").write(data)
+    for c in TRAINED:
+        w = os.path.join(out_dir, f"trained_{c['name']}.bin")
+        B, T = tok.shape
+        res = {}
+        for mode in ("chunk", "step"):
+            of = os.path.join(tmp, f"lg_{mode}.f32")
+            run([os.path.join(REF, "ref_logits"), w, c["backbone"], str(c["d_model"]), str(c["n_layers"]),
+                 tf, str(B), str(T), mode, of])
+            res[mode] = np.fromfile(of, np.float32).reshape(B, T, 256)
+        np.savez_compressed(os.path.join(out_dir, f"ref_logits_trained_{c['name']}.npz"),
+                            tokens=tok, chunk=res["chunk"], step=res["step"])
+        boa = os.path.join(tmp, "t.boa")
+        args = [str(c["d_model"]), str(c["n_layers"]), "--backbone", c["backbone"]]
+        run([os.path.join(REF, "boa_constrictor"), "compress", w, fin, boa] + args +
+            ["--gpu-batch", str(TRAINED_DATA["batch"]), "--chunk-size", str(TRAINED_DATA["chunk"])])
+        back = os.path.join(tmp, "t.out")
+        run([os.path.join(REF, "boa_constrictor"), "decompress", w, boa, back] + args +
+            ["--gpu-batch", str(TRAINED_DATA["batch"])])
+        man["trained_result"][c["name"]] = dict(
+            weights_sha=sha(open(w, "rb").read()), input_sha=sha(data), boa_bytes=os.path.getsize(boa),
+            boa_sha=sha(open(boa, "rb").read()), bits_per_byte=8.0 * os.path.getsize(boa) / len(data),
+            ref_roundtrip=open(back, "rb").read() == data)
+    for f in os.listdir(tmp):
+        os.remove(os.path.join(tmp, f))
+    os.rmdir(tmp)
+    json.dump(man, open(os.path.join(out_dir, "manifest.json"), "w"), indent=1)
+    print(json.dumps(man["trained_result"], indent=1))
 
 
 def pyrc_inputs(cfg):
@@ -221,4 +285,6 @@ def main(out_dir):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.path.join(ROOT, "tests", "golden"))
+    args = [a for a in sys.argv[1:] if a != "--trained"]
+    out = args[0] if args else os.path.join(ROOT, "tests", "golden")
+    main_trained(out) if "--trained" in sys.argv else main(out)

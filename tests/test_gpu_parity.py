@@ -172,6 +172,31 @@ def test_roundtrip_and_bits_per_byte_vs_reference(boa, manifest, m256):
     assert abs(bpb - manifest["rand_result"]["bits_per_byte"]) <= 0.005 * manifest["rand_result"]["bits_per_byte"]
 
 
+TRAINED = ["mamba_d64L2", "mamba_d80L1", "mingru_d160L1"]
+
+
+@pytest.mark.parametrize("name", TRAINED)
+def test_trained_checkpoint_logits_and_bits_per_byte(boa, manifest, name):
+    """Weights converted from the reference's trained checkpoints (d_model 64,
+    80 with dt_rank 5, and a d_model 160 minGRU): their predictions are sharply
+    non-uniform, so the logits gate (both forms, 1e-3 of the largest logit)
+    and the bits/byte gate (0.5 % of the reference CLI's container on the same
+    particle records) are strict; the round trip is byte-exact."""
+    c = next(x for x in manifest["trained"] if x["name"] == name)
+    m = boa.Model(os.path.join(GOLDEN, f"trained_{name}.bin"), c["backbone"], c["d_model"], c["n_layers"])
+    z = np.load(os.path.join(GOLDEN, f"ref_logits_trained_{name}.npz"))
+    for mode, key in ((0, "chunk"), (1, "step")):
+        ref = z[key]
+        assert np.abs(m.logits(z["tokens"], mode) - ref).max() <= LOGIT_RTOL * np.abs(ref).max(), key
+    td = manifest["trained_data"]
+    data = boa.synth.particle_stream(td["n_bytes"], td["data_seed"])
+    fb, sizes, pay = _roundtrip(boa, m, data, td["chunk"])
+    blob = boa.boa2_build(len(data), td["chunk"], fb, sizes, pay)
+    ref = manifest["trained_result"][name]
+    assert ref["ref_roundtrip"]
+    assert abs(len(blob) - ref["boa_bytes"]) <= 0.005 * ref["boa_bytes"]
+
+
 @pytest.mark.parametrize("n,chunk,batch,tile", [(1, 64, 0, 0), (2, 64, 0, 0), (1001, 250, 0, 0),
                                                 (1001, 250, 3, 0), (3000, 1000, 2, 7), (4097, 4096, 0, 0)])
 def test_roundtrip_edges(boa, m64, n, chunk, batch, tile):

@@ -9,6 +9,20 @@ from conftest import GOLDEN, dirichlet_cdfs
 LOGIT_CFGS = ["d64L2", "d256L8", "mingru_d64L2", "lstm_d64L2", "gru_d64L2"]
 
 
+@pytest.mark.parametrize("name", ["mamba_d64L2", "mamba_d80L1", "mingru_d160L1"])
+@pytest.mark.parametrize("mode", [0, 1])
+def test_oracle_logits_match_reference_trained(oracle, boa, manifest, name, mode):
+    """The CPU restatement on weights converted from the reference's trained
+    checkpoints (non-uniform predictions, d_model 64 / 80 / 160) against the
+    reference's own logits on the same bytes."""
+    c = next(x for x in manifest["trained"] if x["name"] == name)
+    z = np.load(f"{GOLDEN}/ref_logits_trained_{name}.npz")
+    m = oracle.OracleModel(f"{GOLDEN}/trained_{name}.bin", boa.BACKBONES[c["backbone"]], c["d_model"],
+                           c["n_layers"])
+    ref = z["chunk" if mode == 0 else "step"]
+    assert np.abs(m.logits(z["tokens"], mode) - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
 @pytest.mark.parametrize("cfg", LOGIT_CFGS)
 @pytest.mark.parametrize("mode", [0, 1])
 def test_oracle_logits_match_reference_gpu(oracle, boa, manifest, wdir, cfg, mode):
