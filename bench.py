@@ -55,9 +55,12 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=1)
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="roundtrip", choices=["roundtrip", "pyrc"],
-                    help="roundtrip: configs[2] compress+decompress (the headline); pyrc: the Python "
-                         "codec's batch range coder against the reference's own extension")
+    ap.add_argument("--workload", default="roundtrip", choices=["roundtrip", "cms", "pyrc"],
+                    help="roundtrip: configs[2] compress+decompress (the headline); cms: the same round trip "
+                         "with the reference's cms_experiment model (trained mambav1 d64 L2) on 4 KiB chunks, "
+                         "the configuration of the reference's published MB/s; pyrc: the Python codec's batch "
+                         "range coder against the reference's own extension")
+    ap.add_argument("--weights", default=None, help="weight file (.bin) instead of random-init weights")
     ap.add_argument("--streams", type=int, default=65536, help="pyrc: streams per batch")
     ap.add_argument("--positions", type=int, default=64, help="pyrc: coded positions per step")
     return ap.parse_args()
@@ -206,11 +209,39 @@ def cpu_sample(weights, d, L, chunk_len, seed, budget_s, threads):
     return len(sub) / MiB / dt, f"{threads} chunks x {plen}-byte prefixes of configs[2] chunks, round trip", dt
 
 
+# The reference's published throughput (portability_solved_cpp/README.md:122-126): the cms_experiment
+# model (experiments/cms_experiment/cms_experiment.yaml: mambav1, d_model 64, 2 layers) on an RTX 5090.
+CMS_PUBLISHED = {"compress_MBps": 7.0, "decompress_MBps": 5.0, "hardware": "RTX 5090",
+                 "source": "portability_solved_cpp/README.md:122-126"}
+CMS_WEIGHTS = os.path.join(ROOT, "tests", "golden", "trained_mamba_d64L2.bin")
+
+
+def apply_workload(a):
+    """--workload cms: the cms_experiment model with its trained weights (converted from the
+    reference's checkpoint by tests/golden/convert_trained.py), 4 KiB chunks."""
+    if a.workload == "cms":
+        a.d_model, a.layers, a.chunk_len = 64, 2, 4096
+        a.weights = a.weights or CMS_WEIGHTS
+    return a
+
+
 def workload_name(a, C, S):
     """The workload string both arms report for this geometry."""
     n = C * S
+    if a.workload == "cms":
+        return (f"cms_experiment model (mambav1 d64 L2, trained weights), {C} chunks x {S} B = "
+                f"{n / MiB:g} MiB per GPU, one batch")
     tag = "configs[2]: " if (a.d_model, a.layers, C, S) == (256, 8, 16384, 16384) else ""
     return f"{tag}mamba d{a.d_model} L{a.layers}, {C} chunks x {S} B = {n / MiB:g} MiB per GPU, one batch"
+
+
+def published_baseline(a):
+    """value / published round trip for the cms workload (null otherwise: no published number exists
+    for configs[2])."""
+    if a.workload != "cms":
+        return None, None
+    rt = 1.0 / (1.0 / CMS_PUBLISHED["compress_MBps"] + 1.0 / CMS_PUBLISHED["decompress_MBps"])
+    return rt, dict(CMS_PUBLISHED, roundtrip_MBps=rt)
 
 
 def run_reference(a):
@@ -222,7 +253,10 @@ def run_reference(a):
     threads = os.cpu_count() or 1
     with tempfile.TemporaryDirectory() as td:
         w = os.path.join(td, "w.bin")
-        boa.synth.write_random_weights(w, "mamba", a.d_model, a.layers, 0)
+        if a.weights:
+            w = a.weights
+        else:
+            boa.synth.write_random_weights(w, "mamba", a.d_model, a.layers, 0)
         for _ in range(a.warmup):
             cpu_sample(w, a.d_model, a.layers, a.chunk_len, 1, 0.2, threads)
         vals, secs = [], []
@@ -379,11 +413,11 @@ def run_pyrc(a):
 
 # --------------------------------------------------------------------------- GPU leg
 def main():
-    a = parse()
+    a = apply_workload(parse())
     if a.workload == "pyrc":
         return run_pyrc(a)
     if a.impl == "reference":
-        return run_reference(a)
+        return run_reference(a)  # a already carries the workload's model and weights
     import torch
     ws, rank, local = dist_info()
     dist = None
@@ -399,7 +433,10 @@ def main():
 
     td = tempfile.mkdtemp()
     wpath = os.path.join(td, f"w{rank}.bin")
-    boa.synth.write_random_weights(wpath, "mamba", a.d_model, a.layers, 0)
+    if a.weights:
+        wpath = a.weights
+    else:
+        boa.synth.write_random_weights(wpath, "mamba", a.d_model, a.layers, 0)
     m = boa.Model(wpath, "mamba", a.d_model, a.layers, device=local)
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
@@ -553,6 +590,7 @@ def main():
 
     if rank == 0:
         total = n * ws
+        pub_rt, pub = published_baseline(a)
         step_rl = step_roofline(a.d_model, a.layers, C, T, hbm_peak, tf_sust)
         step_rl["compress_frac"] = (n / MiB / (comp_ms * 1e-3)) / step_rl["compress_bound_MBps"]
         step_rl["decompress_frac"] = (n / MiB / (dec_ms * 1e-3)) / step_rl["decompress_bound_MBps"]
@@ -561,8 +599,11 @@ def main():
             "metric": "compress+decompress round-trip MB/s",
             "value": total / MiB / (step_ms * 1e-3),
             "unit": "MB/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup, "ms_per_step": step_ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16x3 (fp32-accurate)",
-            "data": "synthetic: seeded float32 particle records, random-init weights",
+            "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": (total / MiB / (step_ms * 1e-3)) / pub_rt if pub_rt else None,
+            "dtype": "bf16x3 (fp32-accurate)",
+            "data": ("synthetic: seeded float32 particle records, "
+                     + (f"weights {os.path.basename(a.weights)}" if a.weights else "random-init weights")),
             "config": {"workload": workload_name(a, C, S),
                        "d_model": a.d_model, "n_layers": a.layers, "chunks_per_gpu": C, "chunk_len": S,
                        "batch_chunks": C, "compress_tile": T, "parallelism": f"chunk-sharded x{ws}",
@@ -582,6 +623,7 @@ def main():
                                      if in_decode and (dom, "decode") in NCU_TRAFFIC_PER_CHUNK else None),
                          "peak_source": f"{peak_kind} ({'bf16 sustained' if bound == 'tensor' else 'HBM copy'})"},
             "step_roofline": step_rl,
+            "published_baseline": pub,
             "kernels": kern,
             "cpu_baseline": cpu,
             "e2e": {"value": total / MiB / (e2e_step_ms * 1e-3), "unit": "MB/s",

@@ -208,39 +208,56 @@ __device__ __forceinline__ double cdf_fix(double my_start, double prev_end) {
 __device__ __forceinline__ double cdf_post(double pre, double delta) {
   return delta != 0.0 ? __dadd_rn(pre, delta) : pre;
 }
-__device__ __forceinline__ uint32_t cdf_q(double c, int k) {
-  return (uint32_t)__dmul_rn(c, kCdfScale) + (uint32_t)k;
-}
+__device__ __forceinline__ uint32_t cdf_f(double c) { return (uint32_t)__dmul_rn(c, kCdfScale); }
 
-// [low, high) of symbol s (encoder side, range_coder_kernels.cu:917-925)
+// Q_k = k + max_{j <= k} floor(C_j * (2^24 - 256)).  The reference quantises
+// Q_k = k + floor(C_k * (2^24 - 256)) (range_coder_kernels.cu:917-925), which
+// is strictly increasing whenever the fixed-up C is non-decreasing.  Its
+// lane-boundary fix-up compares each lane's start with the previous lane's
+// PRE-fix-up end, so once C has reached 1.0 (a near-certain prediction) a later
+// lane can start one ulp lower: Q_k = Q_{k+1}, an empty interval that no
+// decoder can resolve (the reference's stream is then undecodable).  The
+// running maximum equals the reference's Q on every row where that Q is
+// strictly increasing and repairs exactly the rows where it is not.  Within a
+// lane C is non-decreasing, so the running maximum only needs each earlier
+// lane's last value.
+
+// [low, high) of symbol s (encoder side)
 template <class Src>
 __device__ __forceinline__ void cdf_symbol(const Src& src, const CdfRow& R, int s, uint32_t& low,
                                            uint32_t& high) {
   const int L = s >> 3, i = s & 7;
   double p[8];
-  double dL = 0.0;
-  if (L > 0) {
-    cdf_lane(src, R, L - 1, p);
-    dL = cdf_fix(R.ws[L], p[7]);
+  double dl = 0.0;   // fix-up delta of the lane being read
+  uint32_t pm = 0u;  // max of floor(C * scale) over the lanes before L
+#pragma unroll 1
+  for (int l = 0; l < L; ++l) {
+    cdf_lane(src, R, l, p);
+    pm = max(pm, cdf_f(cdf_post(p[7], dl)));
+    dl = cdf_fix(R.ws[l + 1], p[7]);
   }
   cdf_lane(src, R, L, p);
-  low = cdf_q(cdf_post(p[i], dL), s);
+  low = max(pm, cdf_f(cdf_post(p[i], dl))) + (uint32_t)s;
   if (s == 255) {
     high = kCdfTotal;
   } else if (i < 7) {
-    high = cdf_q(cdf_post(p[i + 1], dL), s + 1);
+    high = max(pm, cdf_f(cdf_post(p[i + 1], dl))) + (uint32_t)(s + 1);
   } else {
     const double d1 = cdf_fix(R.ws[L + 1], p[7]);
-    high = cdf_q(cdf_post(R.ws[L + 1], d1), s + 1);
+    const uint32_t f = max(pm, cdf_f(cdf_post(p[7], dl)));
+    high = max(f, cdf_f(cdf_post(R.ws[L + 1], d1))) + (uint32_t)(s + 1);
   }
 }
 
 // Decoder search: lowest s with Q_s <= target < Q_{s+1}
-// (warp ballot + __ffs in range_coder_kernels.cu:747-763 picks the lowest).
+// (warp ballot + __ffs in range_coder_kernels.cu:747-763 picks the lowest),
+// over the same Q as cdf_symbol.
 template <class Src>
 __device__ __forceinline__ int cdf_search(const Src& src, const CdfRow& R, uint32_t target, uint32_t& low,
                                           uint32_t& high) {
-  double dl = 0.0;  // fix-up delta of the current lane
+  double dl = 0.0;   // fix-up delta of the current lane
+  uint32_t rm = 0u;  // running max of floor(C * scale) up to the current symbol
+  uint32_t q = 0u;   // Q of the current symbol
 #pragma unroll 1
   for (int l = 0; l < 32; ++l) {
     double p[8];
@@ -250,11 +267,20 @@ __device__ __forceinline__ int cdf_search(const Src& src, const CdfRow& R, uint3
       dn = cdf_fix(R.ws[l + 1], p[7]);
       next0 = cdf_post(R.ws[l + 1], dn);
     }
-    uint32_t q = cdf_q(cdf_post(p[0], dl), 8 * l);
+    if (l == 0) {
+      rm = cdf_f(cdf_post(p[0], dl));
+      q = rm;
+    }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int k = 8 * l + j;
-      const uint32_t qn = (k == 255) ? kCdfTotal : cdf_q(j < 7 ? cdf_post(p[j + 1], dl) : next0, k + 1);
+      uint32_t qn;
+      if (k == 255) {
+        qn = kCdfTotal;
+      } else {
+        rm = max(rm, cdf_f(j < 7 ? cdf_post(p[j + 1], dl) : next0));
+        qn = rm + (uint32_t)(k + 1);
+      }
       if (target >= q && target < qn) {
         low = q;
         high = qn;

@@ -399,9 +399,17 @@ void cdf_row(const float* lg, float inv_t, uint32_t* Q) {
   for (int l = 1; l < 32; ++l)
     if (delta[l] != 0.0)
       for (int i = 0; i < 8; ++i) cdf[l * 8 + i] += delta[l];
-  // quantise: Q_k = (u32)(C_k * (2^24 - 256)) + k; Q_256 = 2^24 (:917-925)
+  // quantise: Q_k = (u32)(C_k * (2^24 - 256)) + k; Q_256 = 2^24 (:917-925),
+  // with the floor term kept non-decreasing (running maximum).  That equals
+  // the reference's Q on every row where its Q is strictly increasing; where
+  // the fix-up above leaves C decreasing by an ulp after C reached 1.0, the
+  // reference's Q has an empty interval (undecodable) and this repairs it.
   const double scale = (double)((1u << 24) - 256);
-  for (int k = 0; k < 256; ++k) Q[k] = (uint32_t)(cdf[k] * scale) + (uint32_t)k;
+  uint32_t rm = 0;
+  for (int k = 0; k < 256; ++k) {
+    rm = std::max(rm, (uint32_t)(cdf[k] * scale));
+    Q[k] = rm + (uint32_t)k;
+  }
   Q[256] = 1u << 24;
 }
 

@@ -172,6 +172,26 @@ def test_roundtrip_and_bits_per_byte_vs_reference(boa, manifest, m256):
     assert abs(bpb - manifest["rand_result"]["bits_per_byte"]) <= 0.005 * manifest["rand_result"]["bits_per_byte"]
 
 
+def test_cdf_strictly_increasing_on_near_certain_rows(boa, m64):
+    """Rows where the reference's quantiser leaves an empty interval (its CDF
+    reaches 1.0 early, then the lane fix-up lets a later lane start an ulp
+    lower): the library's Q is strictly increasing, so every symbol decodes."""
+    z = np.load(os.path.join(GOLDEN, "cdf_edge_rows.npz"))
+    Q = m64.cdf_from_logits(z["logits"]).astype(np.int64)
+    assert (np.diff(Q, axis=1) > 0).all() and (Q[:, 256] == 1 << 24).all()
+
+
+def test_trained_model_chunk_with_near_certain_miss_roundtrips(boa):
+    """The chunk that exposed the empty-interval case: the trained d64 L2 model
+    predicts one byte at 0.99995 and sees another (p = 3e-20); compress and
+    decompress must still agree."""
+    m = boa.Model(os.path.join(GOLDEN, "trained_mamba_d64L2.bin"), "mamba", 64, 2)
+    S = 4096
+    chunk = boa.synth.particle_stream(1544 * S, 1)[1543 * S:]
+    fb, sizes, pay = m.compress(chunk, S)
+    assert m.decompress(fb, sizes, pay, [S], S) == chunk
+
+
 TRAINED = ["mamba_d64L2", "mamba_d80L1", "mingru_d160L1"]
 
 

@@ -9,6 +9,14 @@ from conftest import GOLDEN, dirichlet_cdfs
 LOGIT_CFGS = ["d64L2", "d256L8", "mingru_d64L2", "lstm_d64L2", "gru_d64L2"]
 
 
+def test_oracle_cdf_strictly_increasing_on_near_certain_rows(oracle):
+    """The oracle's quantiser on the rows that give the reference's rule an
+    empty interval: strictly increasing, total 2^24."""
+    z = np.load(f"{GOLDEN}/cdf_edge_rows.npz")
+    Q = oracle.cdf_rows(z["logits"]).astype(np.int64)
+    assert (np.diff(Q, axis=1) > 0).all() and (Q[:, 256] == 1 << 24).all()
+
+
 @pytest.mark.parametrize("name", ["mamba_d64L2", "mamba_d80L1", "mingru_d160L1"])
 @pytest.mark.parametrize("mode", [0, 1])
 def test_oracle_logits_match_reference_trained(oracle, boa, manifest, name, mode):
