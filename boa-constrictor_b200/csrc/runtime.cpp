@@ -1031,21 +1031,28 @@ int boa_model_logits(boa_model* m, const uint8_t* tokens, int B, int L, int mode
   if (!tokens || !logits || B <= 0 || L <= 0 || (mode != 0 && mode != 1))
     return fail(m, BOA_E_INVALID, "bad logits arguments");
   StreamScope scope(m);
-  const size_t rows = mode == 0 ? (size_t)B * L : (size_t)B;
-  if (int rc = ensure_work(m, rows, B, 1)) return rc;
-  const size_t lbytes = (size_t)B * L * 256 * 4;
-  uint8_t* d_tok = (uint8_t*)ensure_io(m, lbytes + (size_t)B * L + 256);
+  // compress form: tiles of up to 64 positions with the state carried between
+  // them, as compress runs (the scan tile's shared memory bounds a tile)
+  const int T = mode == 0 ? std::min(L, 64) : 1;
+  if (int rc = ensure_work(m, (size_t)B * T, B, 1)) return rc;
+  const size_t tok_b = ((size_t)B * L + 255) & ~size_t(255);
+  uint8_t* d_tok = (uint8_t*)ensure_io(m, tok_b + (size_t)B * T * 256 * 4);
   if (!d_tok) return fail(m, BOA_E_NOMEM, "staging allocation failed");
-  float* d_lg = (float*)(d_tok + (((size_t)B * L + 255) & ~size_t(255)));
+  float* d_lg = (float*)(d_tok + tok_b);
   cudaStream_t st = m->own;
   BOA_CK(cudaMemcpyAsync(d_tok, tokens, (size_t)B * L, cudaMemcpyHostToDevice, st));
   if (int rc = reset_states(m, B)) return rc;
   if (mode == 0) {
-    boa::TokenSrc src{0, d_tok, 0, 0, 0, L, nullptr};
-    boa::GemmArgs h{};
-    h.out_f32 = d_lg; h.ld_f32 = 256;
-    if (int rc = forward(m, src, B, L, boa::EPI_LOGITS, h)) return rc;
-    BOA_CK(cudaMemcpyAsync(logits, d_lg, lbytes, cudaMemcpyDeviceToHost, st));
+    for (int t0 = 0; t0 < L; t0 += T) {
+      const int Tt = std::min(T, L - t0);
+      boa::TokenSrc src{1, d_tok, (long long)B * L, L, t0, Tt, nullptr, (long long)L, nullptr, nullptr};
+      boa::GemmArgs h{};
+      h.out_f32 = d_lg; h.ld_f32 = 256;
+      if (int rc = forward(m, src, B, Tt, boa::EPI_LOGITS, h)) return rc;
+      // rows (b, tau) of the tile -> logits[b][t0 + tau]
+      BOA_CK(cudaMemcpy2DAsync(logits + (size_t)t0 * 256, (size_t)L * 256 * 4, d_lg, (size_t)Tt * 256 * 4,
+                               (size_t)Tt * 256 * 4, (size_t)B, cudaMemcpyDeviceToHost, st));
+    }
   } else {
     // step form: token column t of every chunk, one row per chunk
     uint8_t* d_col = (uint8_t*)m->lf;  // B bytes of scratch

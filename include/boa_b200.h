@@ -144,8 +144,10 @@ uint64_t boa_launch_count(const boa_model* h);
 
 /* ---- model outputs for parity testing ------------------------------------
  * Logits [B][L][256] (head bias included) of B fresh chunks of L tokens.
- * mode 0 runs the compress form (all L positions per launch, as
- * BoaPredictorGPU::forward_chunk, boa_gpu.hpp:1081-1102); mode 1 runs the
+ * mode 0 runs the compress form (tiles of up to 64 positions per launch
+ * with the state carried between them, as compress does and as
+ * BoaPredictorGPU::forward_chunk with --tile, boa_gpu.hpp:1081-1102); any L is
+ * accepted.  mode 1 runs the
  * decompress form (L single-position steps, as step_batch,
  * boa_gpu.hpp:1034-1053).  Host buffers. */
 int boa_model_logits(boa_model* h, const uint8_t* tokens, int B, int L, int mode, float* logits);

@@ -132,7 +132,7 @@ def test_logits_vs_oracle_d256L8(boa, oracle, m256, weights):
     assert rel <= LOGIT_RTOL, rel
 
 
-@pytest.mark.parametrize("B,L", [(1, 5), (3, 130), (130, 3)])
+@pytest.mark.parametrize("B,L", [(1, 5), (3, 130), (130, 3), (2, 1100)])
 def test_compress_and_decompress_forms_bitwise_equal(boa, m256, B, L):
     """The decoder regenerates the encoder's CDFs only if the step form
     (M = chunks) and the tile form (M = chunks x positions) agree bitwise."""
