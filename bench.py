@@ -206,7 +206,7 @@ def cpu_sample(weights, d, L, chunk_len, seed, budget_s, threads):
     out = m.decompress(fb, st, len(sub), plen, threads=threads)
     dt = time.perf_counter() - t
     assert out == sub
-    return len(sub) / MiB / dt, f"{threads} chunks x {plen}-byte prefixes of configs[2] chunks, round trip", dt
+    return len(sub) / MiB / dt, f"{threads} chunks x {plen}-byte prefixes of the workload's chunks, round trip", dt
 
 
 # The reference's published throughput (portability_solved_cpp/README.md:122-126): the cms_experiment
