@@ -10,7 +10,7 @@ convert_boa_weights.py) on three of the C++-compatible checkpoints in
 experiments/cms_experiment/ and writes tests/golden/trained_<name>.bin.
 Unlike random-init weights these predict sharply non-uniform byte
 distributions, so logits and bits/byte comparisons against the reference
-are strict.  The widths cover d_model 64 and 80 (Mamba, dt_rank 4 and 5) and
+are strict.  The widths cover d_model 64, 80 and 128 (Mamba, dt_rank 4, 5 and 8) and
 160 (minGRU).
 """
 import os
@@ -22,6 +22,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 TRAINED = {
     "mamba_d64L2": ("cms_experiment_final_model_fp32_mambav1_64_2_20ep.pt", "mamba", 64, 2),
     "mamba_d80L1": ("cms_experiment_final_model_fp32_mambav1_80_1_20.pt", "mamba", 80, 1),
+    "mamba_d128L1": ("cms_experiment_final_model_fp32_128dm_mambav1.pt", "mamba", 128, 1),
     "mingru_d160L1": ("cms_experiment_final_model_fp32_160MinGRU.pt", "mingru", 160, 1),
 }
 

@@ -68,6 +68,7 @@ PYRC = [dict(name="k256", seed=21, N=48, T=160, K=256, alpha=0.1),
 # trained checkpoints (tests/golden/trained_<name>.bin, see convert_trained.py)
 TRAINED = [dict(name="mamba_d64L2", backbone="mamba", d_model=64, n_layers=2),
            dict(name="mamba_d80L1", backbone="mamba", d_model=80, n_layers=1),
+           dict(name="mamba_d128L1", backbone="mamba", d_model=128, n_layers=1),
            dict(name="mingru_d160L1", backbone="mingru", d_model=160, n_layers=1)]
 TRAINED_DATA = dict(n_bytes=65536, data_seed=41, chunk=4096, batch=16, B=3, T=64)
 

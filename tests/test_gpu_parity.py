@@ -192,7 +192,7 @@ def test_trained_model_chunk_with_near_certain_miss_roundtrips(boa):
     assert m.decompress(fb, sizes, pay, [S], S) == chunk
 
 
-TRAINED = ["mamba_d64L2", "mamba_d80L1", "mingru_d160L1"]
+TRAINED = ["mamba_d64L2", "mamba_d80L1", "mamba_d128L1", "mingru_d160L1"]
 
 
 @pytest.mark.parametrize("name", TRAINED)

@@ -17,7 +17,7 @@ def test_oracle_cdf_strictly_increasing_on_near_certain_rows(oracle):
     assert (np.diff(Q, axis=1) > 0).all() and (Q[:, 256] == 1 << 24).all()
 
 
-@pytest.mark.parametrize("name", ["mamba_d64L2", "mamba_d80L1", "mingru_d160L1"])
+@pytest.mark.parametrize("name", ["mamba_d64L2", "mamba_d80L1", "mamba_d128L1", "mingru_d160L1"])
 @pytest.mark.parametrize("mode", [0, 1])
 def test_oracle_logits_match_reference_trained(oracle, boa, manifest, name, mode):
     """The CPU restatement on weights converted from the reference's trained
