@@ -132,7 +132,11 @@ __device__ __forceinline__ void dec_update(DecState& st, uint32_t low, uint32_t 
 // ---------------------------------------------------------------------------
 // softmax -> CDF for one row held by one thread.
 // Src must provide: __device__ void lane(int l, float (&v)[8]) const
-// returning the 8 logits (bias already added) of symbols 8l..8l+7.
+// returning the 8 logits (bias already added) of symbols 8l..8l+7, and
+// static constexpr bool kCache: when true, cdf_prepare replaces the row's
+// values by their exponentials (put(l, e)) once the maximum is known, and
+// every later walk over the row reads them instead of evaluating __expf again
+// (the same floats, so the same bits).
 // ---------------------------------------------------------------------------
 struct CdfRow {
   float mx;
@@ -163,8 +167,13 @@ __device__ __forceinline__ void cdf_prepare(const Src& src, float inv_t, CdfRow&
     float v[8];
     src.lane(l, v);
     double sd = 0.0;
+    float e[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) sd = __dadd_rn(sd, (double)cdf_exp(v[i], mx, inv_t));
+    for (int i = 0; i < 8; ++i) {
+      e[i] = cdf_exp(v[i], mx, inv_t);
+      sd = __dadd_rn(sd, (double)e[i]);
+    }
+    if constexpr (Src::kCache) src.put(l, e);
     ts[l] = sd;
     R.ws[l] = sd;
   }
@@ -199,7 +208,8 @@ __device__ __forceinline__ void cdf_lane(const Src& src, const CdfRow& R, int l,
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     p[i] = run;
-    run = __dadd_rn(run, __dmul_rn((double)cdf_exp(v[i], R.mx, R.inv_t), R.inv_sum));
+    const float e = Src::kCache ? v[i] : cdf_exp(v[i], R.mx, R.inv_t);
+    run = __dadd_rn(run, __dmul_rn((double)e, R.inv_sum));
   }
 }
 __device__ __forceinline__ double cdf_fix(double my_start, double prev_end) {

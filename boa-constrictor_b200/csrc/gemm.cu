@@ -70,10 +70,15 @@ __device__ __forceinline__ void store_f32x16(float* p, const float (&v)[16]) {
 
 // row source for the CDF code: one logits row staged in shared memory
 struct SmemRow {
-  const float* p;
+  float* p;
+  static constexpr bool kCache = true;  // the row is this thread's own staging copy
   __device__ __forceinline__ void lane(int l, float (&v)[8]) const {
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = p[l * 8 + i];
+  }
+  __device__ __forceinline__ void put(int l, const float (&e)[8]) const {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) p[l * 8 + i] = e[i];
   }
 };
 constexpr int kRowStride = 257;  // floats; odd stride -> conflict-free per-thread rows

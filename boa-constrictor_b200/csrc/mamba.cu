@@ -787,6 +787,8 @@ cudaError_t launch_rc_decode_cdf(DecState* ds, const uint32_t* cdf, const uint32
 // test hook: CDF of logits rows with the shared CDF code (one thread per row)
 struct GlobalRow {
   const float* p;
+  static constexpr bool kCache = false;
+  __device__ __forceinline__ void put(int, const float (&)[8]) const {}
   __device__ __forceinline__ void lane(int l, float (&v)[8]) const {
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = p[l * 8 + i];
