@@ -164,3 +164,38 @@ def test_reference_warm_start_container_fields(boa, boa2, manifest):
     # the reference's own warm-start round trip fails on a real model
     # (recorded by make_golden.py); ours is tested in test_gpu_parity.py
     assert manifest["rand_warm_result"]["ref_roundtrip"] is False
+
+
+def test_container_property_roundtrip(boa, boa2):
+    """For arbitrary chunk geometries, stream sizes (including empty streams
+    and streams long enough for multi-byte length varints), warm-start flags
+    and first bytes: the library's writer equals the container restatement
+    byte for byte, and the library's parser returns every field unchanged."""
+    from hypothesis import given, settings, strategies as st
+
+    @settings(max_examples=60, deadline=None, derandomize=True)
+    @given(n=st.integers(1, 40), chunk=st.integers(1, 70000), last=st.integers(1, 70000),
+           warm=st.integers(0, 5), seed=st.integers(0, 2**31 - 1))
+    def check(n, chunk, last, warm, seed):
+        last = min(last, chunk)
+        rng = np.random.default_rng(seed)
+        sizes = rng.integers(0, 300, n).astype(np.uint32)
+        sizes[rng.random(n) < 0.2] = 0
+        pay = rng.integers(0, 2**32, int(sizes.sum()), dtype=np.uint64).astype(np.uint32)
+        fb = rng.integers(0, 256, n).astype(np.uint8)
+        total = (n - 1) * chunk + last
+        streams, o = [], 0
+        for s in sizes:
+            streams.append(pay[o:o + s].tobytes())
+            o += int(s)
+        w = warm if warm else 0
+        blob = boa.boa2_build(total, chunk, fb, sizes, pay, warm_start=w)
+        assert blob == boa2.build(total, chunk, fb, streams, warm_start=bool(w), interleave_batch=w)
+        p = boa.boa2_parse(blob)
+        assert (p["total_size"], p["chunk_len"], p["n_chunks"], p["last_chunk_len"]) == (total, chunk, n, last)
+        assert p["streams"] == streams and np.array_equal(p["first_bytes"], fb)
+        assert p["flags"] == (1 if w else 0)
+        if w:
+            assert p["interleave_batch"] == w
+
+    check()
