@@ -181,6 +181,20 @@ def test_cdf_strictly_increasing_on_near_certain_rows(boa, m64):
     assert (np.diff(Q, axis=1) > 0).all() and (Q[:, 256] == 1 << 24).all()
 
 
+def test_cdf_strictly_increasing_on_many_peaked_rows(boa, m64):
+    """The same property on the GPU quantiser over 200k near-certain rows,
+    and the coder round trip of a symbol drawn from each row's tail."""
+    from test_oracle_golden import _peaked_logits
+    rng = np.random.default_rng(6)
+    lg = _peaked_logits(rng, 200000)
+    Q = m64.cdf_from_logits(lg).astype(np.int64)
+    assert (np.diff(Q, axis=1) > 0).all() and (Q[:, 256] == 1 << 24).all()
+    q = Q[:4000].astype(np.uint32).reshape(4000, 1, 257)
+    syms = rng.integers(0, 256, (4000, 1)).astype(np.uint8)
+    sizes, pay = m64.rc_encode_cdf(q, syms)
+    assert np.array_equal(m64.rc_decode_cdf(q, sizes, pay), syms)
+
+
 def test_trained_model_chunk_with_near_certain_miss_roundtrips(boa):
     """The chunk that exposed the empty-interval case: the trained d64 L2 model
     predicts one byte at 0.99995 and sees another (p = 3e-20); compress and
