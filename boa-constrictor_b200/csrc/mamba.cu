@@ -92,50 +92,62 @@ cudaError_t launch_embed_ln(const TokenSrc& src, const float* emb, int d, float*
 }
 
 // ---------------------------------------------------------------- causal conv
-// Thread per (chunk, channel); window = three carried inputs + current.
-// Sum order bias, oldest tap .. newest (mamba_kernels.cu:158-197, :370-412),
-// explicit round-to-nearest operations so every launch shape computes the
-// same bits.
-__global__ void conv_kernel(const float* __restrict__ xz, int di, float* __restrict__ cst,
-                            const float* __restrict__ cw, const float* __restrict__ cb, float* __restrict__ u,
-                            __nv_bfloat16* __restrict__ uhl, long long plane, int B, int T) {
+// Causal depthwise conv (k = 4) + SiLU, window = three carried inputs +
+// current (mamba_kernels.cu:158-197, :370-412); conv_tap fixes the sum order
+// and rounding, so every launch shape computes the same bits.
+// Compress tile: one thread per (chunk, 4 channels) walking the T positions,
+// with 128-bit loads of x and stores of u and 64-bit stores of each bf16
+// plane (d_model is a multiple of 16, so di % 4 == 0).
+__global__ void conv4_kernel(const float* __restrict__ xz, int di, float* __restrict__ cst,
+                             const float* __restrict__ cw, const float* __restrict__ cb, float* __restrict__ u,
+                             __nv_bfloat16* __restrict__ uhl, long long plane, int B, int T) {
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= (long long)B * di) return;
-  const int b = (int)(idx / di), c = (int)(idx - (long long)b * di);
-  float* s = cst + (size_t)b * 3 * di + c;
-  float w0 = s[0], w1 = s[di], w2 = s[2 * di];
-  const float4 k = reinterpret_cast<const float4*>(cw)[c];
-  const float bias = cb[c];
+  const int q = di / 4;
+  if (idx >= (long long)B * q) return;
+  const int b = (int)(idx / q), c = (int)(idx - (long long)b * q) * 4;
+  float4* s = reinterpret_cast<float4*>(cst + (size_t)b * 3 * di + c);
+  float4 w0 = s[0], w1 = s[di / 4], w2 = s[di / 2];
+  const float4* k = reinterpret_cast<const float4*>(cw) + c;
+  const float4 k0 = k[0], k1 = k[1], k2 = k[2], k3 = k[3];
+  const float4 bias = *reinterpret_cast<const float4*>(cb + c);
   constexpr int PB = 8;  // x fetched 8 positions at a time, one batch ahead
   const size_t row0 = (size_t)b * T;
-  float cx[PB], nx[PB];
+  float4 cx[PB], nx[PB];
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-  for (int i = 0; i < PB; ++i) cx[i] = i < T ? xz[(row0 + i) * 2 * di + c] : 0.f;
+  for (int i = 0; i < PB; ++i)
+    cx[i] = i < T ? *reinterpret_cast<const float4*>(xz + (row0 + i) * 2 * di + c) : zero;
   for (int t0 = 0; t0 < T; t0 += PB) {
 #pragma unroll
-    for (int i = 0; i < PB; ++i) nx[i] = t0 + PB + i < T ? xz[(row0 + t0 + PB + i) * 2 * di + c] : 0.f;
+    for (int i = 0; i < PB; ++i)
+      nx[i] = t0 + PB + i < T ? *reinterpret_cast<const float4*>(xz + (row0 + t0 + PB + i) * 2 * di + c) : zero;
 #pragma unroll
     for (int i = 0; i < PB; ++i) {
       if (t0 + i < T) {
         const size_t row = row0 + t0 + i;
-        const float xt = cx[i];
-        const float o = conv_tap(w0, w1, w2, xt, k, bias);
-        u[row * di + c] = o;
-        __nv_bfloat16 h, l;
-        split_bf16(o, h, l);
-        uhl[row * di + c] = h;
-        uhl[plane + row * di + c] = l;
+        const float4 xt = cx[i];
+        float4 o;
+        o.x = conv_tap(w0.x, w1.x, w2.x, xt.x, k0, bias.x);
+        o.y = conv_tap(w0.y, w1.y, w2.y, xt.y, k1, bias.y);
+        o.z = conv_tap(w0.z, w1.z, w2.z, xt.z, k2, bias.z);
+        o.w = conv_tap(w0.w, w1.w, w2.w, xt.w, k3, bias.w);
+        *reinterpret_cast<float4*>(u + row * di + c) = o;
+        __nv_bfloat16 h[4], l[4];
+        split_bf16(o.x, h[0], l[0]); split_bf16(o.y, h[1], l[1]);
+        split_bf16(o.z, h[2], l[2]); split_bf16(o.w, h[3], l[3]);
+        *reinterpret_cast<uint2*>(uhl + row * di + c) = *reinterpret_cast<uint2*>(h);
+        *reinterpret_cast<uint2*>(uhl + plane + row * di + c) = *reinterpret_cast<uint2*>(l);
         w0 = w1; w1 = w2; w2 = xt;
       }
     }
 #pragma unroll
     for (int i = 0; i < PB; ++i) cx[i] = nx[i];
   }
-  s[0] = w0; s[di] = w1; s[2 * di] = w2;
+  s[0] = w0; s[di / 4] = w1; s[di / 2] = w2;
 }
 
 // Decompress step (T = 1): one thread per (chunk, 4 channels), 128-bit
-// accesses; the same conv_tap arithmetic as conv_kernel.
+// accesses; the same conv_tap arithmetic as conv4_kernel.
 __global__ void conv_step4_kernel(const float* __restrict__ xz, int di, float* __restrict__ cst,
                                   const float* __restrict__ cw, const float* __restrict__ cb, float* __restrict__ u,
                                   __nv_bfloat16* __restrict__ uhl, long long plane, int B) {
@@ -163,13 +175,14 @@ __global__ void conv_step4_kernel(const float* __restrict__ xz, int di, float* _
 
 cudaError_t launch_conv(const float* xz, int di, float* cst, const float* cw, const float* cb, float* u,
                         __nv_bfloat16* uhl, long long plane, int B, int T, cudaStream_t st) {
-  if (T == 1 && di % 4 == 0) {
+  if (di % 4 != 0) return cudaErrorInvalidValue;
+  if (T == 1) {
     const long long n4 = (long long)B * (di / 4);
     conv_step4_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(xz, di, cst, cw, cb, u, uhl, plane, B);
     return cudaGetLastError();
   }
-  const long long n = (long long)B * di;
-  conv_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(xz, di, cst, cw, cb, u, uhl, plane, B, T);
+  const long long n4 = (long long)B * (di / 4);
+  conv4_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(xz, di, cst, cw, cb, u, uhl, plane, B, T);
   return cudaGetLastError();
 }
 
