@@ -8,6 +8,10 @@ decompress it again (a byte-exact round trip, verified after timing).
 
   python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference]
   python bench.py --workload pyrc   # the Python codec's batch coder (secondary line)
+  python bench.py --workload cms    # the reference's cms_experiment model (mambav1
+                                    # d64 L2, its trained weights) on 16,384 chunks
+                                    # of 4 KiB: the configuration of the reference's
+                                    # published MB/s, so vs_baseline is set
 
 Under torchrun each rank drives its own GPU with its own 256 MiB shard (weak
 scaling; chunks are independent so no collective touches the data path; the
