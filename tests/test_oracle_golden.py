@@ -205,3 +205,20 @@ def test_oracle_cdf_strictly_increasing_on_peaked_rows(oracle):
     lg = _peaked_logits(np.random.default_rng(5), 20000)
     Q = oracle.cdf_rows(lg).astype(np.int64)
     assert (np.diff(Q, axis=1) > 0).all() and (Q[:, 256] == 1 << 24).all()
+
+
+@pytest.mark.parametrize("name", ["mamba_d64L2", "mamba_d80L1", "mamba_d128L1", "mingru_d160L1"])
+def test_oracle_bits_per_byte_trained_vs_reference(oracle, boa, boa2, manifest, name):
+    """The CPU restatement's container for the trained models on the same
+    64 KiB of particle records: byte-exact round trip, and within 0.5 % of the
+    size of the reference CLI's container."""
+    c = next(x for x in manifest["trained"] if x["name"] == name)
+    td = manifest["trained_data"]
+    data = boa.synth.particle_stream(td["n_bytes"], td["data_seed"])
+    m = oracle.OracleModel(f"{GOLDEN}/trained_{name}.bin", boa.BACKBONES[c["backbone"]], c["d_model"],
+                           c["n_layers"])
+    fb, streams = m.compress(data, td["chunk"])
+    assert m.decompress(fb, streams, len(data), td["chunk"]) == data
+    blob = boa2.build(len(data), td["chunk"], fb, [s.tobytes() for s in streams])
+    ref = manifest["trained_result"][name]["boa_bytes"]
+    assert abs(len(blob) - ref) <= 0.005 * ref
