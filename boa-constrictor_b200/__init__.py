@@ -30,6 +30,7 @@ CLI_PATH = os.path.join(HERE, "bin", "boa_constrictor")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "boa_b200.h")
 
 BOA_OK, BOA_E_INVALID, BOA_E_CUDA, BOA_E_IO, BOA_E_FORMAT, BOA_E_DEVICE, BOA_E_NOMEM = 0, -1, -2, -3, -4, -5, -6
+BOA_STREAM_FAILED = 0xFFFFFFFF  # size of a stream whose coding stopped (handle-free encoders)
 BACKBONES = {"mamba": 0, "mambav1": 0, "lstm": 1, "gru": 2, "mingru": 3}
 PROF_CLASSES = 12
 
@@ -68,6 +69,7 @@ SIGNATURES = {
     "boa_set_stream": (C.c_int, [C.c_void_p, C.c_void_p]),
     "boa_set_batch": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
     "boa_set_warm_start": (C.c_int, [C.c_void_p, C.c_uint32]),
+    "boa_batch_geometry": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_int, _i32p, _i32p]),
     "boa_stream_capacity_words": (C.c_uint32, [C.c_uint32]),
     "boa_compress_chunks": (C.c_int, [C.c_void_p, _u8p, C.c_size_t, C.c_uint32, C.c_uint32, C.c_uint32, _u8p,
                                       _u32p, C.c_size_t, _u32p, _u64p]),
@@ -88,6 +90,14 @@ SIGNATURES = {
     "boa_rc_decode_cdf": (C.c_int, [C.c_void_p, _u32p, C.c_int, C.c_int, _u32p, _u32p, _u8p]),
     "boa_rc_encode_cdf_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_uint32,
                                             C.c_void_p, C.c_void_p]),
+    "boa_rc_state_bytes": (C.c_size_t, [C.c_int]),
+    "boa_rc_encoder_init": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
+    "boa_rc_encode_cdf_steps": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                          C.c_uint32, C.c_void_p]),
+    "boa_rc_encoder_finish": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p, C.c_int, C.c_void_p]),
+    "boa_rc_decoder_init": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
+    "boa_rc_decode_cdf_steps": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                          C.c_void_p, C.c_void_p]),
     "boa_cdf_from_logits": (C.c_int, [C.c_void_p, _f32p, C.c_int, C.c_float, _u32p]),
     "boa_boa2_build": (C.c_int, [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _u8p,
                                  _u64p, _u8p, _u8p, C.c_size_t, C.POINTER(C.c_size_t)]),
@@ -164,6 +174,13 @@ class Model:
 
     def set_batch(self, chunks: int = 0, tile: int = 0):
         _check(lib().boa_set_batch(self.h, chunks, tile), self.h)
+
+    def batch_geometry(self, n_chunks: int, chunk_len: int, compress: bool = True):
+        """-> (chunks per batch, positions per compress tile) the next call would use."""
+        b, t = C.c_int32(), C.c_int32()
+        _check(lib().boa_batch_geometry(self.h, n_chunks, chunk_len, int(bool(compress)), C.byref(b), C.byref(t)),
+               self.h)
+        return b.value, t.value
 
     def set_warm_start(self, interleave_batch: int):
         _check(lib().boa_set_warm_start(self.h, interleave_batch), self.h)

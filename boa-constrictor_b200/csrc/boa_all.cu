@@ -9,4 +9,5 @@
 #include "runtime.cpp"
 #include "container.cpp"
 #include "noalloc.cu"
+#include "coder_api.cu"
 #include "pyrc.cu"

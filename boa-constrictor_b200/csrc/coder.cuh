@@ -28,7 +28,7 @@ struct EncState {  // RCState, gemm_gpu.hpp:115-121
   int inv;             // inverted_num: pending carry-run length
   uint32_t first_inv;  // first_inv_lower_word
   int w;               // words written
-  int pad;
+  int bad;             // coding stopped (empty interval or capacity); finish reports the stream as failed
 };
 struct DecState {  // RCDecState, gemm_gpu.hpp:212-217
   unsigned long long lower, range, point;
@@ -37,7 +37,7 @@ struct DecState {  // RCDecState, gemm_gpu.hpp:212-217
 };
 
 __host__ __device__ __forceinline__ void enc_init(EncState& s) {
-  s.lower = 0ull; s.range = ~0ull; s.inv = 0; s.first_inv = 0u; s.w = 0; s.pad = 0;
+  s.lower = 0ull; s.range = ~0ull; s.inv = 0; s.first_inv = 0u; s.w = 0; s.bad = 0;
 }
 
 // Encode one symbol with CDF slot [left, left+prob) of 2^24.  Returns false

@@ -67,8 +67,9 @@ cudaError_t launch_rms_split(const float* x, int d, const float* w, __nv_bfloat1
 cudaError_t launch_encode_tile(const uint2* lf, EncState* es, uint32_t* pitch_buf, int pitch_words, int B,
                                int T, int t0, long long n_bytes, int chunk_len, long long stride, cudaStream_t st);
 cudaError_t launch_enc_init(EncState* es, int B, cudaStream_t st);
+// failed streams get size failed_size; report = also set the device error word
 cudaError_t launch_enc_finish(EncState* es, uint32_t* pitch_buf, int pitch_words, uint32_t* sizes, int B,
-                              cudaStream_t st);
+                              cudaStream_t st, uint32_t failed_size = 0u, bool report = true);
 // exclusive scan of sizes -> offsets (one block), continuing from offsets[0];
 // total in offsets[B]
 cudaError_t launch_offsets(const uint32_t* sizes, unsigned long long* offsets, int B, cudaStream_t st);
@@ -95,7 +96,8 @@ cudaError_t launch_increment(int* d_t, cudaStream_t st);
 
 // integer-CDF coder (configs[1] style): cdf [n_steps][n_streams][257]
 cudaError_t launch_rc_encode_cdf(EncState* es, const uint32_t* cdf, const uint8_t* syms, int n_streams,
-                                 int n_steps, uint32_t* pitch_buf, int pitch_words, cudaStream_t st);
+                                 int n_steps, uint32_t* pitch_buf, int pitch_words, cudaStream_t st,
+                                 bool report = true);
 cudaError_t launch_rc_decode_init(DecState* ds, const uint32_t* payload, const unsigned long long* offsets,
                                   const uint32_t* sizes, int n_streams, cudaStream_t st);
 cudaError_t launch_rc_decode_cdf(DecState* ds, const uint32_t* cdf, const uint32_t* payload,

@@ -555,11 +555,12 @@ __global__ void encode_tile_kernel(const uint2* __restrict__ lf, EncState* es, u
   if (n <= 0) return;
   if (n > T) n = T;
   EncState s = es[b];
+  if (s.bad) return;
   uint32_t* out = pitch_buf + (size_t)b * pitch;
   const uint2* p = lf + (size_t)b * T;
   for (int i = 0; i < n; ++i) {
     const uint2 v = p[i];
-    if (!enc_symbol(s, v.x, v.y - v.x, out, pitch)) { set_dev_error(BOA_ERR_STREAM_OVERFLOW); break; }
+    if (!enc_symbol(s, v.x, v.y - v.x, out, pitch)) { set_dev_error(BOA_ERR_STREAM_OVERFLOW); s.bad = 1; break; }
   }
   es[b] = s;
 }
@@ -569,17 +570,24 @@ cudaError_t launch_encode_tile(const uint2* lf, EncState* es, uint32_t* pitch_bu
   return cudaGetLastError();
 }
 
-__global__ void enc_finish_kernel(EncState* es, uint32_t* pitch_buf, int pitch, uint32_t* sizes, int B) {
+// Flush every stream.  A stream whose coding stopped (state.bad) or whose
+// flush does not fit gets size `failed_size`; `report` also records the
+// failure in the device error word (handle-based callers read it there,
+// handle-free callers see only the size).
+__global__ void enc_finish_kernel(EncState* es, uint32_t* pitch_buf, int pitch, uint32_t* sizes, int B,
+                                  uint32_t failed_size, int report) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   EncState s = es[b];
-  const int w = enc_finish(s, pitch_buf + (size_t)b * pitch, pitch);
-  if (w < 0) set_dev_error(BOA_ERR_STREAM_OVERFLOW);
-  sizes[b] = w < 0 ? 0u : (uint32_t)w;
+  const int w = s.bad ? -1 : enc_finish(s, pitch_buf + (size_t)b * pitch, pitch);
+  if (w < 0 && !s.bad && report) set_dev_error(BOA_ERR_STREAM_OVERFLOW);
+  if (w < 0) s.bad = 1;
+  sizes[b] = w < 0 ? failed_size : (uint32_t)w;
   es[b] = s;
 }
-cudaError_t launch_enc_finish(EncState* es, uint32_t* pitch_buf, int pitch, uint32_t* sizes, int B, cudaStream_t st) {
-  enc_finish_kernel<<<(B + 255) / 256, 256, 0, st>>>(es, pitch_buf, pitch, sizes, B);
+cudaError_t launch_enc_finish(EncState* es, uint32_t* pitch_buf, int pitch, uint32_t* sizes, int B, cudaStream_t st,
+                              uint32_t failed_size, bool report) {
+  enc_finish_kernel<<<(B + 255) / 256, 256, 0, st>>>(es, pitch_buf, pitch, sizes, B, failed_size, report ? 1 : 0);
   return cudaGetLastError();
 }
 
@@ -729,64 +737,110 @@ cudaError_t launch_increment(int* d_t, cudaStream_t st) {
 
 // ---------------------------------------------------------------- integer-CDF coder
 // Encoder: thread per stream reads only Q[s] and Q[s+1] of each step.
+// A failed stream is marked in its state (and, with `report`, in the device
+// error word) and codes nothing more.
 __global__ void rc_encode_cdf_kernel(EncState* es, const uint32_t* __restrict__ cdf, const uint8_t* __restrict__ syms,
-                                     int n_streams, int n_steps, uint32_t* pitch_buf, int pitch) {
+                                     int n_streams, int n_steps, uint32_t* pitch_buf, int pitch, int report) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n_streams) return;
   EncState s = es[i];
+  if (s.bad) return;
   uint32_t* out = pitch_buf + (size_t)i * pitch;
-  for (int t = 0; t < n_steps; ++t) {
-    const size_t rowi = (size_t)t * n_streams + i;
-    const int sym = syms[rowi];
-    const uint32_t* q = cdf + rowi * 257;
-    const uint32_t lo = q[sym], hi = q[sym + 1];
-    // a caller-supplied CDF must give the coded symbol a non-empty interval
-    // inside [0, 2^24]; anything else would code a stream that cannot decode
-    if (hi <= lo || hi > (1u << 24)) { set_dev_error(BOA_ERR_BAD_INPUT); break; }
-    if (!enc_symbol(s, lo, hi - lo, out, pitch)) { set_dev_error(BOA_ERR_STREAM_OVERFLOW); break; }
+  // the loads do not depend on the coder state: fetch 8 steps' (Q[s], Q[s+1])
+  // pairs before coding them, so 8 scattered reads per thread are in flight
+  constexpr int kAhead = 8;
+  for (int t0 = 0; t0 < n_steps && !s.bad; t0 += kAhead) {
+    uint32_t lo[kAhead], hi[kAhead];
+#pragma unroll
+    for (int j = 0; j < kAhead; ++j) {
+      if (t0 + j < n_steps) {
+        const size_t rowi = (size_t)(t0 + j) * n_streams + i;
+        const int sym = __ldcs(syms + rowi);
+        const uint32_t* q = cdf + rowi * 257;
+        lo[j] = __ldcs(q + sym);
+        hi[j] = __ldcs(q + sym + 1);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kAhead; ++j) {
+      if (t0 + j >= n_steps || s.bad) break;
+      // a caller-supplied CDF must give the coded symbol a non-empty interval
+      // inside [0, 2^24]; anything else would code a stream that cannot decode
+      if (hi[j] <= lo[j] || hi[j] > (1u << 24)) { if (report) set_dev_error(BOA_ERR_BAD_INPUT); s.bad = 1; break; }
+      if (!enc_symbol(s, lo[j], hi[j] - lo[j], out, pitch)) {
+        if (report) set_dev_error(BOA_ERR_STREAM_OVERFLOW);
+        s.bad = 1;
+        break;
+      }
+    }
   }
   es[i] = s;
 }
 cudaError_t launch_rc_encode_cdf(EncState* es, const uint32_t* cdf, const uint8_t* syms, int n_streams, int n_steps,
-                                 uint32_t* pitch_buf, int pitch, cudaStream_t st) {
-  rc_encode_cdf_kernel<<<(n_streams + 127) / 128, 128, 0, st>>>(es, cdf, syms, n_streams, n_steps, pitch_buf, pitch);
+                                 uint32_t* pitch_buf, int pitch, cudaStream_t st, bool report) {
+  rc_encode_cdf_kernel<<<(n_streams + 127) / 128, 128, 0, st>>>(es, cdf, syms, n_streams, n_steps, pitch_buf, pitch,
+                                                                report ? 1 : 0);
   return cudaGetLastError();
 }
 
-// Decoder: one warp per stream.  Lane l reads Q[8l .. 8l+8] (coalesced
-// 1 KB row), tests its 8 symbols, and a ballot picks the lowest match, as the
-// reference's warp search does (range_coder_kernels.cu:743-763).  The coder
-// state is kept warp-uniform (every lane applies the same update).
-__global__ void rc_decode_cdf_kernel(DecState* ds, const uint32_t* __restrict__ cdf, const uint32_t* __restrict__ payload,
-                                     const unsigned long long* __restrict__ off, int n_streams, int n_steps,
-                                     uint8_t* __restrict__ syms) {
+// Decoder: one warp per stream.  Lane l holds Q[l + 32k] (k = 0..8; Q[256]
+// on lane 0 only), so each of the nine loads of a row is one coalesced
+// 128-byte access, and the next step's row is loaded before the current
+// step's search so the two overlap.  The search returns what the reference's
+// warp search returns (range_coder_kernels.cu:743-763): the lowest s with
+// Q[s] <= target < Q[s+1] -- each lane tests its entries against their
+// successors (Q[s+1] is lane l+1's entry k, or lane 0's entry k+1 for
+// l = 31) and a warp minimum picks the lowest hit.  No hit decodes symbol 0
+// with an empty interval, as there.  The coder state is warp-uniform.
+__device__ __forceinline__ void dec_row_load(const uint32_t* __restrict__ q, int lane, uint32_t (&v)[9]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) v[k] = __ldcs(q + lane + 32 * k);
+  v[8] = lane == 0 ? __ldcs(q + 256) : 0u;
+}
+__global__ void __launch_bounds__(256) rc_decode_cdf_kernel(DecState* ds, const uint32_t* __restrict__ cdf,
+                                                            const uint32_t* __restrict__ payload,
+                                                            const unsigned long long* __restrict__ off, int n_streams,
+                                                            int n_steps, uint8_t* __restrict__ syms) {
   const int i = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (i >= n_streams) return;
   DecState s = ds[i];
   const uint32_t* in = payload + off[i];
+  uint32_t v[9];
+  dec_row_load(cdf + (size_t)i * 257, lane, v);
   for (int t = 0; t < n_steps; ++t) {
     const size_t rowi = (size_t)t * n_streams + i;
-    const uint32_t* q = cdf + rowi * 257;
-    uint32_t v[9];
-#pragma unroll
-    for (int j = 0; j < 9; ++j) v[j] = q[lane * 8 + j];  // Q[256] read by lane 31 only is the total
+    uint32_t nv[9];
+    if (t + 1 < n_steps) dec_row_load(cdf + (rowi + n_streams) * 257, lane, nv);
     const uint32_t target = dec_target(s);
-    int hit = -1;
+    // successor of entry (lane, k): lane+1's entry k, or lane 0's entry k+1
+    int best = 1 << 30;
 #pragma unroll
-    for (int j = 7; j >= 0; --j)
-      if (target >= v[j] && target < v[j + 1]) hit = j;
-    const unsigned ball = __ballot_sync(0xffffffffu, hit >= 0);
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t up = __shfl_down_sync(0xffffffffu, v[k], 1);
+      const uint32_t wrap = __shfl_sync(0xffffffffu, v[k + 1], 0);
+      const uint32_t nxt = lane == 31 ? wrap : up;
+      if (target >= v[k] && target < nxt && best == (1 << 30)) best = lane + 32 * k;
+    }
+    best = __reduce_min_sync(0xffffffffu, best);
     int sym = 0;
     uint32_t lo = 0, hi = 0;
-    if (ball) {
-      const int wl = __ffs(ball) - 1;
-      sym = wl * 8 + __shfl_sync(0xffffffffu, hit, wl);
-      lo = q[sym];
-      hi = q[sym + 1];
+    if (best != (1 << 30)) {
+      sym = best;
+      const int k = sym >> 5, kn = (sym + 1) >> 5;
+      uint32_t a = v[0], b = v[0];
+#pragma unroll
+      for (int j = 1; j < 9; ++j) {  // warp-uniform register selects, no local memory
+        if (j == k) a = v[j];
+        if (j == kn) b = v[j];
+      }
+      lo = __shfl_sync(0xffffffffu, a, sym & 31);
+      hi = __shfl_sync(0xffffffffu, b, (sym + 1) & 31);
     }
     if (lane == 0) syms[rowi] = (uint8_t)sym;
     dec_update(s, lo, hi, in);
+#pragma unroll
+    for (int k = 0; k < 9; ++k) v[k] = nv[k];
   }
   if (lane == 0) ds[i] = s;
 }

@@ -58,9 +58,10 @@ extern "C" int boa_rc_encode_cdf_noalloc(const uint32_t* d_cdf, const uint8_t* d
   // the array keeps the previous call's states: reset every stream used here
   if ((e = boa::launch_enc_init(es, n_streams, st)) != cudaSuccess ||
       (n_steps > 0 &&
-       (e = boa::launch_rc_encode_cdf(es, d_cdf, d_syms, n_streams, n_steps, d_words, (int)pitch_words, st)) !=
-           cudaSuccess) ||
-      (e = boa::launch_enc_finish(es, d_words, (int)pitch_words, d_sizes, n_streams, st)) != cudaSuccess)
+       (e = boa::launch_rc_encode_cdf(es, d_cdf, d_syms, n_streams, n_steps, d_words, (int)pitch_words, st,
+                                      false)) != cudaSuccess) ||
+      (e = boa::launch_enc_finish(es, d_words, (int)pitch_words, d_sizes, n_streams, st, BOA_STREAM_FAILED, false)) !=
+          cudaSuccess)
     return fail(nullptr, BOA_E_CUDA, std::string("boa_rc_encode_cdf_noalloc launch: ") + cudaGetErrorString(e));
   return BOA_OK;
 }

@@ -754,6 +754,21 @@ int boa_set_batch(boa_model* m, int chunks, int tile) {
   return 0;
 }
 
+int boa_batch_geometry(boa_model* m, uint32_t n_chunks, uint32_t chunk_len, int compress, int* chunks, int* tile) {
+  if (!m || !chunks || !tile || n_chunks == 0 || chunk_len == 0) return BOA_E_INVALID;
+  DeviceGuard dev(m->device);
+  int B, T;
+  if (m->warm) {
+    B = (int)std::min<uint32_t>(m->warm, n_chunks);
+    T = compress ? std::max(1, std::min<int>(m->cfg_tile > 0 ? m->cfg_tile : 64, (int)std::max<uint32_t>(1, chunk_len - 1))) : 1;
+  } else {
+    pick_batch(m, n_chunks, chunk_len, compress != 0, B, T);
+  }
+  *chunks = B;
+  *tile = T;
+  return 0;
+}
+
 uint64_t boa_device_bytes(const boa_model* m) {
   return m ? (uint64_t)(m->wbytes + m->work_bytes + m->io_bytes) : 0;
 }

@@ -119,13 +119,15 @@ def write_random_weights(path: str, backbone: str = "mamba", d_model: int = 256,
     return write_weights(path, random_weights(backbone, d_model, n_layers, seed, std=std), fp16=fp16)
 
 
-def particle_stream(n_bytes: int, seed: int) -> bytes:
-    """Little-endian float32 particle records (8 fields, 32 bytes each)."""
+_BLOCK_RECORDS = 1 << 20
+
+
+def _particle_blocks(n_bytes: int, seed: int):
+    """Yield the stream's blocks of 2**20 records as little-endian f4 [nb, 8]."""
     rng = np.random.default_rng(seed)
     n_rec = (n_bytes + 31) // 32
-    blocks = []
-    for start in range(0, n_rec, 1 << 20):
-        nb = min(1 << 20, n_rec - start)
+    for start in range(0, n_rec, _BLOCK_RECORDS):
+        nb = min(_BLOCK_RECORDS, n_rec - start)
         pt = rng.exponential(30.0, nb)
         eta = rng.uniform(-2.5, 2.5, nb)
         phi = rng.uniform(-math.pi, math.pi, nb)
@@ -133,9 +135,46 @@ def particle_stream(n_bytes: int, seed: int) -> bytes:
         charge = rng.integers(0, 2, nb) * 2 - 1
         cov = np.round(rng.normal(0.0, 1.0, (3, nb)), 3)
         rec = np.stack([pt, eta, phi, mass, charge, cov[0], cov[1], cov[2]], axis=1)
-        blocks.append(rec.astype("<f4"))
+        yield rec.astype("<f4")
+
+
+def particle_stream(n_bytes: int, seed: int) -> bytes:
+    """Little-endian float32 particle records (8 fields, 32 bytes each)."""
+    blocks = list(_particle_blocks(n_bytes, seed))
     data = np.concatenate(blocks).tobytes() if blocks else b""
     return data[:n_bytes]
+
+
+def particle_windows(total_bytes: int, seed: int, chunk_len: int, first_chunk: int, n_chunks: int,
+                     window: int) -> np.ndarray:
+    """The first ``window`` bytes of chunks [first_chunk, first_chunk + n_chunks)
+    of ``particle_stream(total_bytes, seed)`` cut into ``chunk_len``-byte chunks, as a
+    u8 array [n_chunks, window], without holding the whole stream: the
+    generator walks the stream block by block (the same draws as
+    ``particle_stream``) and keeps only the windows.  Row i equals
+    ``particle_stream(...)[(first_chunk + i) * chunk_len:][:window]`` (zero-padded past the
+    stream's end)."""
+    window = min(window, chunk_len)
+    out = np.zeros((n_chunks, window), np.uint8)
+    c = 0                      # next chunk (relative) whose window is not complete
+    pos = 0                    # stream offset of the start of `carry`
+    carry = np.zeros(0, np.uint8)
+    for blk in _particle_blocks(total_bytes, seed):  # block sizes depend on the total
+        buf = np.concatenate([carry, blk.reshape(-1).view(np.uint8)])
+        top = pos + buf.size
+        while c < n_chunks:
+            s = (first_chunk + c) * chunk_len
+            need = max(0, min(window, total_bytes - s))  # the stream's last chunk may be short
+            if s + need > top:
+                break
+            out[c, :need] = buf[s - pos: s - pos + need]
+            c += 1
+        if c >= n_chunks:
+            break
+        keep = min((first_chunk + c) * chunk_len - pos, buf.size)  # drop what no later window needs
+        carry = buf[keep:]
+        pos += keep
+    return out
 
 
 def exact_logit_weights(d_model: int, n_layers: int, seed: int, support, low: float = -1000.0):
@@ -179,3 +218,33 @@ def markov_stream(n_bytes: int, seed: int, alpha: float = 0.05) -> bytes:
         out[i] = s
         a, b = b, s
     return out.tobytes()
+
+
+def markov_windows(seed: int, n_chunks: int, window: int, alpha: float = 0.05) -> np.ndarray:
+    """configs[3]-scale input from the same order-2 Markov source as
+    ``markov_stream``: the context tables are drawn first from
+    ``default_rng(seed)`` exactly as there, then every chunk is its own run of
+    the chain from context (0, 0), all chunks advanced together one position
+    at a time (uniforms drawn [window, n_chunks]).  Returns u8 [n_chunks,
+    window].  A single 256 MiB sequential stream would take hours in Python;
+    the per-chunk runs have the same transition law."""
+    rng = np.random.default_rng(seed)
+    g = rng.gamma(alpha, 1.0, size=(65536, 256))
+    g /= g.sum(axis=1, keepdims=True)
+    cdf = np.cumsum(g, axis=1)
+    # every row offset by its context index, so one sorted array serves all
+    # rows: a draw in context r searches r + u * cdf[r][-1]
+    ctx = np.arange(65536, dtype=np.float64)
+    flat = (cdf + ctx[:, None]).reshape(-1)
+    last = cdf[:, -1]
+    out = np.empty((n_chunks, window), np.uint8)
+    a = np.zeros(n_chunks, np.int64)
+    b = np.zeros(n_chunks, np.int64)
+    for t in range(window):
+        u = rng.random(n_chunks)
+        r = (a << 8) | b
+        s = np.searchsorted(flat, r + u * last[r], side="right") - r * 256
+        s = np.clip(s, 0, 255)
+        out[:, t] = s
+        a, b = b, s
+    return out

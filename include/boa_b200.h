@@ -32,6 +32,12 @@ extern "C" {
 #define BOA_E_DEVICE (-5)    /* device-side check failed (wait timeout, stream overflow) */
 #define BOA_E_NOMEM (-6)     /* device allocation failed */
 
+/* Size written by the handle-free encoders (boa_rc_encoder_finish,
+ * boa_rc_encode_cdf_noalloc) for a stream whose coding stopped: a coded
+ * symbol had an empty interval or one above 2^24, or the stream outgrew its
+ * pitch.  Such a stream's words are not a decodable stream. */
+#define BOA_STREAM_FAILED 0xFFFFFFFFu
+
 #define BOA_BACKBONE_MAMBA 0 /* gemm_gpu.hpp BackboneType: mamba (mambav1 blocks) */
 #define BOA_BACKBONE_LSTM 1   /* LSTMBlockGPU (boa_gpu.hpp:365-502) */
 #define BOA_BACKBONE_GRU 2    /* GRUBlockGPU (boa_gpu.hpp:504-600) */
@@ -72,6 +78,12 @@ int boa_set_stream(boa_model* h, void* cuda_stream);
  * (--tile, boa.cpp:313-316).  0 = automatic from free device memory
  * (auto_size_params, boa.cpp:109-156). */
 int boa_set_batch(boa_model* h, int chunks_per_batch, int tile_tokens);
+/* The batch the next compress (compress != 0) or decompress call over
+ * n_chunks chunks of chunk_len bytes would run: chunks per batch and positions
+ * per compress tile (1 for decompress), as auto_size_params (boa.cpp:109-156)
+ * reports them before a run.  Allocates nothing. */
+int boa_batch_geometry(boa_model* h, uint32_t n_chunks, uint32_t chunk_len, int compress, int* chunks_per_batch,
+                       int* tile_tokens);
 /* --warm-start (boa.cpp:313-319, :395-435, :608-610): with interleave_batch
  * W > 0 the codec runs W lanes; lane b codes chunks b*S, b*S+1, ... with
  * S = ceil(n_chunks / W), carrying the model state from chunk to chunk (each
@@ -180,11 +192,40 @@ int boa_rc_decode_cdf(boa_model* h, const uint32_t* cdf, int n_streams, int n_st
  * synchronised.  The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress), so make it before any stream capture.
  * Every call shares the array and resets the states it uses: calls that
- * overlap on the GPU race.  Errors are reported by boa_last_error(NULL);
- * the device-side checks (stream capacity, empty CDF interval) land in the
- * device's error word, read and cleared by the next boa_sync() on it. */
+ * overlap on the GPU race.  Argument and launch errors are returned (message
+ * in boa_last_error(NULL)).  A stream whose coding stopped on the device (an
+ * empty or out-of-range CDF interval, a full pitch) gets d_sizes[i] =
+ * BOA_STREAM_FAILED; the other streams are unaffected, and no model handle's
+ * error state is touched. */
 int boa_rc_encode_cdf_noalloc(const uint32_t* d_cdf, const uint8_t* d_syms, int n_streams, int n_steps,
                               uint32_t* d_words, uint32_t pitch_words, uint32_t* d_sizes, void* stream);
+/* ---- the same coder, step-wise on caller-owned device state ---------------
+ * Replace gpu_rc_init (range_coder_kernels.cu:46-60), the per-position
+ * encode launches (:234-275), gpu_rc_finish_batch (:279-317),
+ * gpu_rc_init_decoder (:319-340) and the per-position decode launches
+ * (:479-490), on explicit integer CDFs instead of logits.  No handle and no
+ * allocation: every pointer is a device pointer the caller owns, states hold
+ * boa_rc_state_bytes(decoder) bytes per stream, and each call only enqueues
+ * kernels on `stream` (NULL = legacy default stream).  A call codes n_steps
+ * positions: cdf [n_steps][n_streams][257] (Q[256] = 2^24), symbols
+ * [n_steps][n_streams]; successive calls continue the streams.  Encoder
+ * stream i is written to d_words + i*pitch_words; the pitch must hold the
+ * whole stream (boa_stream_capacity_words(total steps + 1) is enough).  A
+ * stream whose coding stops (empty or out-of-range interval, full pitch) is
+ * marked in its state and gets size BOA_STREAM_FAILED from finish.  The
+ * decoder reads stream i at d_words + d_offsets[i] (word offsets: i*pitch for
+ * the encoder's layout, or a compacted BOA2 payload's offsets) and writes
+ * symbols [n_steps][n_streams]. */
+size_t boa_rc_state_bytes(int decoder);
+int boa_rc_encoder_init(void* d_states, int n_streams, void* stream);
+int boa_rc_encode_cdf_steps(void* d_states, const uint32_t* d_cdf, const uint8_t* d_syms, int n_streams, int n_steps,
+                            uint32_t* d_words, uint32_t pitch_words, void* stream);
+int boa_rc_encoder_finish(void* d_states, uint32_t* d_words, uint32_t pitch_words, uint32_t* d_sizes, int n_streams,
+                          void* stream);
+int boa_rc_decoder_init(void* d_states, const uint32_t* d_words, const uint64_t* d_offsets, const uint32_t* d_sizes,
+                        int n_streams, void* stream);
+int boa_rc_decode_cdf_steps(void* d_states, const uint32_t* d_cdf, int n_streams, int n_steps, const uint32_t* d_words,
+                            const uint64_t* d_offsets, uint8_t* d_syms, void* stream);
 /* The integer CDF the library derives from one or more logits rows
  * ([rows][256] -> [rows][257]); exposes the quantiser of
  * range_coder_kernels.cu:860-925 for testing.  Host buffers. */

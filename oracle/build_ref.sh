@@ -7,11 +7,13 @@
 #   _gpu_range_cuda_ext*.so  the Python codec's batch range coder: importing
 #                    gpu_range_coder.py compiles it (gpu_range_coder.py:14-367);
 #                    TMPDIR points its build folder into _ref
-# Needs the reference checkout ($BOA_REF_DIR, or the default below); without
-# it the script does nothing and says so.  Outputs are git-ignored.
+# usage: build_ref.sh [reference checkout]
+# The checkout is the first argument, else $BOA_REF_DIR, else a folder named
+# "reference" beside this repository; without it the script does nothing and
+# says so.  Outputs are git-ignored.
 set -euo pipefail
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
-REF="${BOA_REF_DIR:-/root/reference}/portability_solved_cpp"
+REF="${1:-${BOA_REF_DIR:-$HERE/../../reference}}/portability_solved_cpp"
 OUT="$HERE/_ref"
 if [ ! -f "$REF/boa.cpp" ]; then echo "reference sources not found at $REF; skipping"; exit 0; fi
 mkdir -p "$OUT"

@@ -22,6 +22,10 @@ manifest.json, so only reference OUTPUTS are stored):
                          reference's bits/byte
   manifest.json          parameters, sizes, sha256, reference round-trip flags
 
+With --configs4 it writes only ref_logits_d512L16.npz (the configs[4] model,
+Mamba d512 / 16 layers, seed 3, both forms) and the reference CLI's container
+size for 32 KiB of particle records under it, merged into manifest.json.
+
 With --trained it writes only the trained-checkpoint fixtures (weights
 converted by convert_trained.py) and merges them into manifest.json:
   ref_logits_trained_<name>.npz  tokens (bytes of the particle stream) and
@@ -285,7 +289,61 @@ def main(out_dir):
     print(json.dumps(man, indent=1))
 
 
+# configs[4] model (Mamba d512 / 16 layers, seed 3) at full depth
+CONFIGS4_LOGITS = dict(name="d512L16", d_model=512, n_layers=16, seed=3, B=2, T=32, tok_seed=9)
+CONFIGS4_DATA = dict(n_bytes=32768, data_seed=4, chunk=4096, batch=8)
+
+
+def main_configs4(out_dir):
+    """--configs4: the reference's logits of the configs[4] model in both forms
+    (ref_logits_d512L16.npz, appended to manifest "logits") and the size of the
+    reference CLI's container of 32 KiB of particle records under it
+    (manifest "configs4_result")."""
+    tmp = os.path.join(out_dir, "_tmp")
+    os.makedirs(tmp, exist_ok=True)
+    man = json.load(open(os.path.join(out_dir, "manifest.json")))
+    c = CONFIGS4_LOGITS
+    w = os.path.join(tmp, "w_c4.bin")
+    synth.write_random_weights(w, "mamba", c["d_model"], c["n_layers"], c["seed"])
+    tok = np.random.default_rng(c["tok_seed"]).integers(0, 256, (c["B"], c["T"]), dtype=np.uint8)
+    tf = os.path.join(tmp, "tok.u8")
+    tok.tofile(tf)
+    res = {}
+    for mode in ("chunk", "step"):
+        of = os.path.join(tmp, f"lg_{mode}.f32")
+        run([os.path.join(REF, "ref_logits"), w, "mamba", str(c["d_model"]), str(c["n_layers"]),
+             tf, str(c["B"]), str(c["T"]), mode, of])
+        res[mode] = np.fromfile(of, np.float32).reshape(c["B"], c["T"], 256)
+    np.savez_compressed(os.path.join(out_dir, f"ref_logits_{c['name']}.npz"),
+                        tokens=tok, chunk=res["chunk"], step=res["step"])
+    man["logits"] = [x for x in man["logits"] if x["name"] != c["name"]] + [c]
+    D = CONFIGS4_DATA
+    data = synth.particle_stream(D["n_bytes"], D["data_seed"])
+    fin = os.path.join(tmp, "c4.in"); open(fin, "wb").write(data)
+    boa = os.path.join(tmp, "c4.boa")
+    args = [str(c["d_model"]), str(c["n_layers"])]
+    run([os.path.join(REF, "boa_constrictor"), "compress", w, fin, boa] + args +
+        ["--gpu-batch", str(D["batch"]), "--chunk-size", str(D["chunk"])])
+    back = os.path.join(tmp, "c4.out")
+    run([os.path.join(REF, "boa_constrictor"), "decompress", w, boa, back] + args + ["--gpu-batch", str(D["batch"])])
+    man["configs4_data"] = D
+    man["configs4_result"] = dict(input_sha=sha(data), boa_bytes=os.path.getsize(boa),
+                                  bits_per_byte=8.0 * os.path.getsize(boa) / len(data),
+                                  ref_roundtrip=open(back, "rb").read() == data)
+    for f in os.listdir(tmp):
+        os.remove(os.path.join(tmp, f))
+    os.rmdir(tmp)
+    json.dump(man, open(os.path.join(out_dir, "manifest.json"), "w"), indent=1)
+    print(json.dumps(man["configs4_result"], indent=1))
+
+
 if __name__ == "__main__":
-    args = [a for a in sys.argv[1:] if a != "--trained"]
+    flags = {"--trained", "--configs4"}
+    args = [a for a in sys.argv[1:] if a not in flags]
     out = args[0] if args else os.path.join(ROOT, "tests", "golden")
-    main_trained(out) if "--trained" in sys.argv else main(out)
+    if "--trained" in sys.argv:
+        main_trained(out)
+    elif "--configs4" in sys.argv:
+        main_configs4(out)
+    else:
+        main(out)

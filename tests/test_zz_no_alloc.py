@@ -6,7 +6,9 @@ must keep a fixed memory footprint -- use this entry point: it keeps its only
 scratch (the per-stream coder states) in a static device array and writes into
 buffers the caller owns.  Its streams must equal those of the regular
 boa_rc_encode_cdf bit for bit, on consecutive calls (the static array keeps the
-previous call's contents, so each call must reset what it uses).
+previous call's contents, so each call must reset what it uses).  A stream
+whose coding stops on the device is reported to this handle-free caller by its
+size (BOA_STREAM_FAILED), never through a model handle's error state.
 
 This file is named to be collected last; it must also pass alone in a fresh
 process.
@@ -46,6 +48,81 @@ def test_noalloc_encoder_matches_allocating_encoder_twice(boa, weights):
         for i in range(ns):
             assert np.array_equal(words[i, :sizes[i]], pay_ref[o:o + sizes[i]])
             o += int(sizes[i])
+
+
+def _noalloc(boa, Q, syms, pitch, words=None, sizes=None):
+    import torch
+    dev = torch.device("cuda", 0)
+    nt, ns = syms.shape
+    d_q = torch.from_numpy(np.ascontiguousarray(Q, np.uint32).view(np.int32)).to(dev)
+    d_s = torch.from_numpy(np.ascontiguousarray(syms)).to(dev)
+    d_w = words if words is not None else torch.full((ns * pitch,), -1, dtype=torch.int32, device=dev)
+    d_n = sizes if sizes is not None else torch.full((ns,), 7, dtype=torch.int32, device=dev)
+    rc = boa.lib().boa_rc_encode_cdf_noalloc(C.c_void_p(d_q.data_ptr()), C.c_void_p(d_s.data_ptr()), ns, nt,
+                                             C.c_void_p(d_w.data_ptr()), pitch, C.c_void_p(d_n.data_ptr()), None)
+    torch.cuda.synchronize()
+    return rc, d_w, d_n
+
+
+def test_noalloc_failed_stream_is_marked_and_handles_stay_clean(boa, weights):
+    """An empty interval in stream 1 marks that stream's size BOA_STREAM_FAILED;
+    the other streams still equal the allocating encoder's, and a model handle
+    on the same device syncs clean afterwards (the failure is not left in the
+    device error word for it)."""
+    m = boa.Model(weights("mamba", 64, 2, 3), "mamba", 64, 2)
+    rng = np.random.default_rng(5)
+    Q, syms = dirichlet_cdfs(rng, 120, 4)
+    bad = Q.copy()
+    s0 = int(syms[30, 1])
+    bad[30, 1, s0 + 1] = bad[30, 1, s0]
+    pitch = boa.capacity_words(121)
+    rc, d_w, d_n = _noalloc(boa, bad, syms, pitch)
+    assert rc == 0
+    sizes = d_n.cpu().numpy().view(np.uint32)
+    assert sizes[1] == boa.BOA_STREAM_FAILED
+    ref_sizes, ref_pay = m.rc_encode_cdf(Q, syms)
+    words = d_w.cpu().numpy().view(np.uint32).reshape(4, pitch)
+    o = 0
+    for i in range(4):
+        if i != 1:
+            assert sizes[i] == ref_sizes[i] and np.array_equal(words[i, :sizes[i]], ref_pay[o:o + sizes[i]])
+        o += int(ref_sizes[i])
+    m.sync()  # raises if the failure had been left in the device error word
+
+
+def test_noalloc_edges_and_no_allocation(boa):
+    """n_steps = 0 gives empty streams (size 0); a pitch one word below
+    boa_stream_capacity_words(n_steps + 1) is rejected; repeated calls leave
+    the device's free memory unchanged."""
+    import torch
+    Q, syms = dirichlet_cdfs(np.random.default_rng(8), 64, 300)
+    pitch = boa.capacity_words(65)
+    dev = torch.device("cuda", 0)
+    q1 = torch.zeros(257, dtype=torch.int32, device=dev)  # valid pointers; nothing is read at n_steps = 0
+    s1 = torch.zeros(1, dtype=torch.uint8, device=dev)
+    w0 = torch.full((300 * pitch,), -1, dtype=torch.int32, device=dev)
+    n0 = torch.full((300,), 7, dtype=torch.int32, device=dev)
+    rc = boa.lib().boa_rc_encode_cdf_noalloc(C.c_void_p(q1.data_ptr()), C.c_void_p(s1.data_ptr()), 300, 0,
+                                             C.c_void_p(w0.data_ptr()), pitch, C.c_void_p(n0.data_ptr()), None)
+    torch.cuda.synchronize()
+    assert rc == 0 and np.all(n0.cpu().numpy() == 0)
+    rc = boa.lib().boa_rc_encode_cdf_noalloc(C.c_void_p(16), C.c_void_p(16), 300, 64, C.c_void_p(16), pitch - 1,
+                                             C.c_void_p(16), None)
+    assert rc == boa.BOA_E_INVALID and b"pitch" in boa.lib().boa_last_error(None)
+    d_w = torch.empty(300 * pitch, dtype=torch.int32, device=dev)
+    d_n = torch.empty(300, dtype=torch.int32, device=dev)
+    _noalloc(boa, Q, syms, pitch, d_w, d_n)  # warm-up: module and symbol already resident after this
+    d_q = torch.from_numpy(Q.view(np.int32)).to(dev)
+    d_s = torch.from_numpy(syms).to(dev)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info(0)[0]
+    for _ in range(3):
+        rc = boa.lib().boa_rc_encode_cdf_noalloc(C.c_void_p(d_q.data_ptr()), C.c_void_p(d_s.data_ptr()), 300, 64,
+                                                 C.c_void_p(d_w.data_ptr()), pitch, C.c_void_p(d_n.data_ptr()), None)
+        assert rc == 0
+    torch.cuda.synchronize()
+    free1 = torch.cuda.mem_get_info(0)[0]
+    assert free1 == free0, (free0, free1, free0 - free1)
 
 
 def test_noalloc_encoder_rejects_oversize(boa):
