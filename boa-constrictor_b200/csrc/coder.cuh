@@ -109,10 +109,22 @@ __device__ __forceinline__ void dec_init(DecState& st, const uint32_t* in, int n
     st.point = (st.point << 32) | (unsigned long long)w;
   }
 }
+// min((point - lower) / scale, 2^24 - 1) with scale = range >> 24, as the
+// reference computes it (range_coder_kernels.cu:765-768), without a 64-bit
+// integer division: range is normalised to [2^32, 2^64), so scale lies in
+// [2^8, 2^40); a single-precision estimate of the quotient (relative error
+// a few 2^-24, i.e. off by at most a few units below 2^24) is corrected by
+// exact 64-bit multiply-compare steps to the exact floor.
 __device__ __forceinline__ uint32_t dec_target(const DecState& st) {
   const unsigned long long scale = st.range >> 24;
-  unsigned long long q = (st.point - st.lower) / scale;
-  if (q >= (1ull << 24)) q = (1ull << 24) - 1ull;
+  const unsigned long long diff = st.point - st.lower;
+  if (diff >= (scale << 24)) return (1u << 24) - 1u;  // quotient >= 2^24: clamped
+  float est = __fdividef((float)diff, (float)scale);
+  est = fminf(fmaxf(est, 0.0f), 16777215.0f);
+  unsigned long long q = (unsigned long long)est;
+  unsigned long long prod = q * scale;  // < 2^64: q < 2^24, scale < 2^40
+  while (prod > diff) { --q; prod -= scale; }
+  while (diff - prod >= scale) { ++q; prod += scale; }
   return (uint32_t)q;
 }
 __device__ __forceinline__ void dec_update(DecState& st, uint32_t low, uint32_t high, const uint32_t* in) {

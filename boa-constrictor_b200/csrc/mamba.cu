@@ -783,19 +783,20 @@ cudaError_t launch_rc_encode_cdf(EncState* es, const uint32_t* cdf, const uint8_
   return cudaGetLastError();
 }
 
-// Decoder: one warp per stream.  Lane l holds Q[l + 32k] (k = 0..8; Q[256]
-// on lane 0 only), so each of the nine loads of a row is one coalesced
-// 128-byte access, and the next step's row is loaded before the current
-// step's search so the two overlap.  The search returns what the reference's
-// warp search returns (range_coder_kernels.cu:743-763): the lowest s with
-// Q[s] <= target < Q[s+1] -- each lane tests its entries against their
-// successors (Q[s+1] is lane l+1's entry k, or lane 0's entry k+1 for
-// l = 31) and a warp minimum picks the lowest hit.  No hit decodes symbol 0
-// with an empty interval, as there.  The coder state is warp-uniform.
-__device__ __forceinline__ void dec_row_load(const uint32_t* __restrict__ q, int lane, uint32_t (&v)[9]) {
+// Decoder: one warp per stream.  Lane l holds Q[l + 32k] (k = 0..7), so each
+// of the eight loads of a row is one coalesced 128-byte access, and the next
+// step's row is loaded before the current step's search so the two overlap.
+// Search: the decoded symbol is the s with Q[s] <= target < Q[s+1]
+// (range_coder_kernels.cu:743-763).  For a non-decreasing CDF the entries
+// <= target are exactly Q[0..s], so every lane counts its entries <= target
+// and one warp reduction gives s + 1; Q[256] = 2^24 exceeds every target.
+// (The reference's lowest-match rule agrees with this on every
+// non-decreasing CDF, which includes every CDF the encoder can code.)  A
+// count of 0 (Q[0] > target) decodes symbol 0 with an empty interval, as the
+// reference's no-match path does.  The coder state is warp-uniform.
+__device__ __forceinline__ void dec_row_load(const uint32_t* __restrict__ q, int lane, uint32_t (&v)[8]) {
 #pragma unroll
   for (int k = 0; k < 8; ++k) v[k] = __ldcs(q + lane + 32 * k);
-  v[8] = lane == 0 ? __ldcs(q + 256) : 0u;
 }
 __global__ void __launch_bounds__(256) rc_decode_cdf_kernel(DecState* ds, const uint32_t* __restrict__ cdf,
                                                             const uint32_t* __restrict__ payload,
@@ -806,41 +807,38 @@ __global__ void __launch_bounds__(256) rc_decode_cdf_kernel(DecState* ds, const 
   if (i >= n_streams) return;
   DecState s = ds[i];
   const uint32_t* in = payload + off[i];
-  uint32_t v[9];
+  uint32_t v[8];
   dec_row_load(cdf + (size_t)i * 257, lane, v);
   for (int t = 0; t < n_steps; ++t) {
     const size_t rowi = (size_t)t * n_streams + i;
-    uint32_t nv[9];
+    uint32_t nv[8];
     if (t + 1 < n_steps) dec_row_load(cdf + (rowi + n_streams) * 257, lane, nv);
     const uint32_t target = dec_target(s);
-    // successor of entry (lane, k): lane+1's entry k, or lane 0's entry k+1
-    int best = 1 << 30;
+    unsigned cnt = 0;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const uint32_t up = __shfl_down_sync(0xffffffffu, v[k], 1);
-      const uint32_t wrap = __shfl_sync(0xffffffffu, v[k + 1], 0);
-      const uint32_t nxt = lane == 31 ? wrap : up;
-      if (target >= v[k] && target < nxt && best == (1 << 30)) best = lane + 32 * k;
-    }
-    best = __reduce_min_sync(0xffffffffu, best);
+    for (int k = 0; k < 8; ++k) cnt += v[k] <= target ? 1u : 0u;
+    const int c = (int)__reduce_add_sync(0xffffffffu, cnt);
     int sym = 0;
     uint32_t lo = 0, hi = 0;
-    if (best != (1 << 30)) {
-      sym = best;
+    if (c > 0) {
+      sym = c - 1;
       const int k = sym >> 5, kn = (sym + 1) >> 5;
       uint32_t a = v[0], b = v[0];
 #pragma unroll
-      for (int j = 1; j < 9; ++j) {  // warp-uniform register selects, no local memory
+      for (int j = 1; j < 8; ++j) {  // warp-uniform register selects, no local memory
         if (j == k) a = v[j];
         if (j == kn) b = v[j];
       }
       lo = __shfl_sync(0xffffffffu, a, sym & 31);
       hi = __shfl_sync(0xffffffffu, b, (sym + 1) & 31);
+      if (sym == 255) hi = __ldg(cdf + rowi * 257 + 256);
     }
     if (lane == 0) syms[rowi] = (uint8_t)sym;
     dec_update(s, lo, hi, in);
+    if (t + 1 < n_steps) {
 #pragma unroll
-    for (int k = 0; k < 9; ++k) v[k] = nv[k];
+      for (int k = 0; k < 8; ++k) v[k] = nv[k];
+    }
   }
   if (lane == 0) ds[i] = s;
 }

@@ -109,7 +109,7 @@ def test_cdf_general_logits_close(boa, oracle, m64):
 
 
 # ---------------------------------------------------------------- model logits
-@pytest.mark.parametrize("cfg", ["d64L2", "d256L8", "mingru_d64L2", "lstm_d64L2", "gru_d64L2"])
+@pytest.mark.parametrize("cfg", ["d64L2", "d256L8", "d512L16", "mingru_d64L2", "lstm_d64L2", "gru_d64L2"])
 def test_logits_vs_reference_golden(boa, oracle, manifest, weights, cfg):
     c = next(x for x in manifest["logits"] if x["name"] == cfg)
     z = np.load(f"{GOLDEN}/ref_logits_{cfg}.npz")
@@ -401,6 +401,32 @@ def test_d512_logits_forms_and_roundtrip(boa, oracle, weights):
     assert np.array_equal(lg, m.logits(tok, 1))
     data = boa.synth.particle_stream(3 * 700 + 5, 4)
     _roundtrip(boa, m, data, 700)
+
+
+def test_configs4_d512_L16_full_depth(boa, oracle, manifest, weights):
+    """configs[4] at its full depth (Mamba d512 / 16 layers, seed 3): logits
+    against the reference's own (ref_logits_d512L16.npz, both of its forms)
+    and the oracle within 1e-3, the compress and decompress forms bitwise
+    equal, a byte-exact round trip of 32 KiB of particle records (seed 4) and
+    its container within 0.5 % of the reference CLI's size."""
+    c = next(x for x in manifest["logits"] if x["name"] == "d512L16")
+    z = np.load(f"{GOLDEN}/ref_logits_d512L16.npz")
+    p = weights("mamba", c["d_model"], c["n_layers"], c["seed"])
+    m = boa.Model(p, "mamba", c["d_model"], c["n_layers"])
+    lg0 = m.logits(z["tokens"], 0)
+    lg1 = m.logits(z["tokens"], 1)
+    assert np.array_equal(lg0, lg1)
+    for ref in (z["chunk"], z["step"]):
+        rel = np.abs(lg0 - ref).max() / np.abs(ref).max()
+        assert rel <= LOGIT_RTOL, rel
+    orc = oracle.OracleModel(p, 0, c["d_model"], c["n_layers"]).logits(z["tokens"], 0)
+    assert np.abs(lg0 - orc).max() <= LOGIT_RTOL * np.abs(orc).max()
+    D, R = manifest["configs4_data"], manifest["configs4_result"]
+    data = boa.synth.particle_stream(D["n_bytes"], D["data_seed"])
+    m.set_batch(D["batch"], 0)
+    fb, sizes, pay = _roundtrip(boa, m, data, D["chunk"])
+    blob = boa.boa2_build(len(data), D["chunk"], fb, sizes, pay)
+    assert abs(len(blob) - R["boa_bytes"]) <= 0.005 * R["boa_bytes"], (len(blob), R["boa_bytes"])
 
 
 def test_fp16_weight_file(boa, oracle, wdir):

@@ -6,7 +6,7 @@ import pytest
 from conftest import GOLDEN, dirichlet_cdfs
 
 
-LOGIT_CFGS = ["d64L2", "d256L8", "mingru_d64L2", "lstm_d64L2", "gru_d64L2"]
+LOGIT_CFGS = ["d64L2", "d256L8", "d512L16", "mingru_d64L2", "lstm_d64L2", "gru_d64L2"]
 
 
 def test_oracle_cdf_strictly_increasing_on_near_certain_rows(oracle):
