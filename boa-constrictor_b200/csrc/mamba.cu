@@ -237,6 +237,24 @@ __device__ __forceinline__ float scan_update(const float4* __restrict__ dl4, con
   return __fmul_rn(y, __fdividef(z, __fadd_rn(1.0f, __expf(-z))));  // y * silu(z)
 }
 
+// Selective-scan state layout, shared by both forms: the di channels of a
+// chunk are cut into slices of W (a divisor of di), and each (chunk, slice)
+// holds its 16 state rows of W floats contiguously, so the decode form moves
+// one contiguous block per work item.  W = di keeps the plain [chunk][16][di]
+// order.
+__host__ __device__ __forceinline__ size_t scan_state_offset(long long b, int c, int di, int W) {
+  return (size_t)b * 16 * di + (size_t)(c / W) * 16 * W + (size_t)(c % W);
+}
+// Slices of at most 256 channels: measured on B200 with 16384 chunks, the
+// decode scan takes 189 / 200 / 224 us at W = 256 / 512 / 128 (d_model 256)
+// and 387 / 407 us at W = 256 / 512 (d_model 512, 0.93 of the HBM copy rate).
+constexpr int kScanSliceMax = 256;
+int scan_slice_width(int di) {
+  int W = di;
+  while (W > kScanSliceMax && W % 2 == 0) W /= 2;
+  return W;
+}
+
 // Compress form: thread per (chunk, channel), h[16] in registers across the T
 // rows of the tile; the chunk's delta rows are staged in shared memory.
 template <int R>
@@ -244,7 +262,8 @@ __global__ void __launch_bounds__(128, 5) scan_tile_kernel(const float* __restri
                                                         const float* __restrict__ dtb, const float* __restrict__ negA,
                                                         const float* __restrict__ Dv, const float* __restrict__ u,
                                                         const float* __restrict__ xz, int di, float* __restrict__ hs,
-                                                        __nv_bfloat16* __restrict__ yhl, long long plane, int T) {
+                                                        __nv_bfloat16* __restrict__ yhl, long long plane, int T,
+                                                        int W) {
   extern __shared__ float sdelta[];  // [T][ld]
   const int b = blockIdx.x;  // chunks on x (y stops at 65535)
   const int c = blockIdx.y * blockDim.x + threadIdx.x;
@@ -259,11 +278,11 @@ __global__ void __launch_bounds__(128, 5) scan_tile_kernel(const float* __restri
 #pragma unroll
   for (int k = 0; k < R / 2; ++k) wdt[k] = reinterpret_cast<const float2*>(dtw + (size_t)c * R)[k];
   float2 na[8], h[8];
-  float* hp = hs + (size_t)b * 16 * di + c;
+  float* hp = hs + scan_state_offset(b, c, di, W);  // rows n at stride W
 #pragma unroll
   for (int p = 0; p < 8; ++p) {
     na[p] = reinterpret_cast<const float2*>(negA + (size_t)c * 16)[p];
-    h[p] = make_float2(hp[(size_t)(2 * p) * di], hp[(size_t)(2 * p + 1) * di]);
+    h[p] = make_float2(hp[(size_t)(2 * p) * W], hp[(size_t)(2 * p + 1) * W]);
   }
   const float bdt = dtb[c], dsk = Dv[c];
   // u and z are fetched in batches of 4 positions, one batch ahead, so each
@@ -301,70 +320,90 @@ __global__ void __launch_bounds__(128, 5) scan_tile_kernel(const float* __restri
     for (int i = 0; i < PB; ++i) { cu[i] = nu[i]; cz[i] = nz[i]; }
   }
 #pragma unroll
-  for (int p = 0; p < 8; ++p) { hp[(size_t)(2 * p) * di] = h[p].x; hp[(size_t)(2 * p + 1) * di] = h[p].y; }
+  for (int p = 0; p < 8; ++p) { hp[(size_t)(2 * p) * W] = h[p].x; hp[(size_t)(2 * p + 1) * W] = h[p].y; }
 }
 
 // Decompress form (T = 1): persistent CTAs stream each chunk's 16 x di state
-// (32 KB at di = 512) through shared memory with bulk async copies, three
-// chunks in flight per CTA, so the kernel runs at HBM rate instead of being
-// bound by per-thread load latency.  One thread per channel.
+// through shared memory with bulk async copies, so the kernel runs at HBM
+// rate instead of being bound by per-thread load latency.  One thread per
+// channel; a CTA covers one slice of W channels (16 x W floats of state per
+// item, 32 KB at W = 512), several CTAs per SM, and each keeps two items in
+// flight ahead of the one it computes.
 constexpr int kScanStages = 3;
 template <int R>
-__global__ void __launch_bounds__(1024) scan_step_kernel(const float* __restrict__ delta, int ld,
-                                                         const float* __restrict__ dtw, const float* __restrict__ dtb,
-                                                         const float* __restrict__ negA, const float* __restrict__ Dv,
-                                                         const float* __restrict__ u, const float* __restrict__ xz,
-                                                         int di, float* __restrict__ hs,
-                                                         __nv_bfloat16* __restrict__ yhl, long long plane, int B) {
+__global__ void __launch_bounds__(512) scan_step_kernel(const float* __restrict__ delta, int ld,
+                                                        const float* __restrict__ dtw, const float* __restrict__ dtb,
+                                                        const float* __restrict__ negA, const float* __restrict__ Dv,
+                                                        const float* __restrict__ u, const float* __restrict__ xz,
+                                                        int di, float* __restrict__ hs,
+                                                        __nv_bfloat16* __restrict__ yhl, long long plane, int B) {
+  // State layout: see scan_state_offset (one contiguous 16 x W block per item).
+  // Work item w = (chunk w / n_sl, channel slice w % n_sl); the block's W
+  // threads own channels sl * W + threadIdx.x.  A stage holds one item: its
+  // 16 state rows (W floats each; one copy when the slice is the whole row),
+  // the u and z slices and the chunk's full delta row.
   extern __shared__ __align__(128) uint8_t sm[];
-  const uint32_t st_bytes = 16u * di * 4, uz_bytes = (uint32_t)di * 4, dl_bytes = ((uint32_t)ld * 4 + 15) & ~15u;
+  const int W = blockDim.x, n_sl = di / W;
+  const uint32_t row_bytes = (uint32_t)W * 4, st_bytes = 16u * row_bytes, uz_bytes = row_bytes;
+  const uint32_t dl_bytes = ((uint32_t)ld * 4 + 15) & ~15u;
   const uint32_t stage_bytes = st_bytes + 2 * uz_bytes + dl_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + kScanStages * stage_bytes);
-  const int c = threadIdx.x;
-  if (c == 0) {
+  const int tid = threadIdx.x;
+  if (tid == 0) {
     for (int s = 0; s < kScanStages; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
   }
   __syncthreads();
+  const long long n_items = (long long)B * n_sl;
+  auto item = [&](int i) { return (long long)blockIdx.x + (long long)i * gridDim.x; };
+  auto state_ptr = [&](long long w) { return hs + (size_t)w * 16 * W; };  // (chunk, slice) blocks in order
   auto issue = [&](int i, int s) {
-    const int b = blockIdx.x + i * gridDim.x;
+    const long long w = item(i);
+    const long long b = w / n_sl;
+    const int c0 = (int)(w % n_sl) * W;
     uint8_t* p = sm + s * stage_bytes;
     mbar_arrive_expect_tx(&full[s], st_bytes + 2 * uz_bytes + (uint32_t)ld * 4);
-    bulk_load(p, hs + (size_t)b * 16 * di, st_bytes, &full[s]);
-    bulk_load(p + st_bytes, u + (size_t)b * di, uz_bytes, &full[s]);
-    bulk_load(p + st_bytes + uz_bytes, xz + (size_t)b * 2 * di + di, uz_bytes, &full[s]);
+    bulk_load(p, state_ptr(w), st_bytes, &full[s]);
+    bulk_load(p + st_bytes, u + (size_t)b * di + c0, uz_bytes, &full[s]);
+    bulk_load(p + st_bytes + uz_bytes, xz + (size_t)b * 2 * di + di + c0, uz_bytes, &full[s]);
     bulk_load(p + st_bytes + 2 * uz_bytes, delta + (size_t)b * ld, (uint32_t)ld * 4, &full[s]);
   };
-  const int n_mine = (B - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-  if (c == 0)
-    for (int s = 0; s < kScanStages && s < n_mine; ++s) issue(s, s);
+  const int n_mine = (int)((n_items - (long long)blockIdx.x + gridDim.x - 1) / gridDim.x);
+  // items i + 1 .. i + kScanStages - 1 are in flight while item i is computed;
+  // the stage of item i - 1 is refilled once its state store has been read
+  if (tid == 0)
+    for (int s = 0; s < kScanStages - 1 && s < n_mine; ++s) issue(s, s);
   float2 wdt[R / 2], na[8];
   float bdt = 0.f, dsk = 0.f;
-  if (c < di) {
-#pragma unroll
-    for (int k = 0; k < R / 2; ++k) wdt[k] = reinterpret_cast<const float2*>(dtw + (size_t)c * R)[k];
-#pragma unroll
-    for (int p = 0; p < 8; ++p) na[p] = reinterpret_cast<const float2*>(negA + (size_t)c * 16)[p];
-    bdt = dtb[c];
-    dsk = Dv[c];
-  }
+  int c_prev = -1;
   bool alive = true;
   for (int i = 0; i < n_mine; ++i) {
     const int s = i % kScanStages;
-    const int b = blockIdx.x + i * gridDim.x;
+    const long long w = item(i);
+    const int c = (int)(w % n_sl) * W + tid;
+    if (c != c_prev) {  // per-channel parameters (reloaded only when the slice changes)
+#pragma unroll
+      for (int k = 0; k < R / 2; ++k) wdt[k] = reinterpret_cast<const float2*>(dtw + (size_t)c * R)[k];
+#pragma unroll
+      for (int p = 0; p < 8; ++p) na[p] = reinterpret_cast<const float2*>(negA + (size_t)c * 16)[p];
+      bdt = dtb[c];
+      dsk = Dv[c];
+      c_prev = c;
+    }
     uint8_t* p = sm + s * stage_bytes;
     if (!mbar_wait(&full[s], (i / kScanStages) & 1)) alive = false;
-    if (alive && c < di) {
+    if (alive) {
       float* hsm = reinterpret_cast<float*>(p);
       const float* usm = reinterpret_cast<const float*>(p + st_bytes);
-      const float* zsm = usm + di;
+      const float* zsm = usm + W;
       const float4* dl = reinterpret_cast<const float4*>(p + st_bytes + 2 * uz_bytes);
       float2 h[8];
 #pragma unroll
-      for (int p = 0; p < 8; ++p) h[p] = make_float2(hsm[(2 * p) * di + c], hsm[(2 * p + 1) * di + c]);
-      const float o = scan_update<R>(dl, wdt, bdt, na, h, usm[c], zsm[c], dsk);
+      for (int q = 0; q < 8; ++q) h[q] = make_float2(hsm[(2 * q) * W + tid], hsm[(2 * q + 1) * W + tid]);
+      const float o = scan_update<R>(dl, wdt, bdt, na, h, usm[tid], zsm[tid], dsk);
 #pragma unroll
-      for (int p = 0; p < 8; ++p) { hsm[(2 * p) * di + c] = h[p].x; hsm[(2 * p + 1) * di + c] = h[p].y; }
+      for (int q = 0; q < 8; ++q) { hsm[(2 * q) * W + tid] = h[q].x; hsm[(2 * q + 1) * W + tid] = h[q].y; }
+      const long long b = w / n_sl;
       __nv_bfloat16 hh, ll;
       split_bf16(o, hh, ll);
       yhl[(size_t)b * di + c] = hh;
@@ -372,35 +411,40 @@ __global__ void __launch_bounds__(1024) scan_step_kernel(const float* __restrict
     }
     fence_proxy_async_smem();
     __syncthreads();
-    if (c == 0) {
+    if (tid == 0) {
       if (alive) {
-        bulk_store(hs + (size_t)b * 16 * di, p, st_bytes);
+        bulk_store(state_ptr(w), p, st_bytes);
         bulk_commit();
       }
-      if (i + kScanStages < n_mine && alive) {
-        bulk_wait_read_all();  // the store must have read the stage before it is refilled
-        issue(i + kScanStages, s);
+      const int nxt = i + kScanStages - 1;
+      if (nxt < n_mine && alive) {
+        bulk_wait_read_1();  // item i - 1's store has read its stage
+        issue(nxt, nxt % kScanStages);
       }
     }
   }
-  if (c == 0) bulk_wait_all();
+  if (tid == 0) bulk_wait_all();
 }
 
 cudaError_t launch_scan(const float* delta, int ld, int r, const float* dtw, const float* dtb, const float* negA,
                         const float* Dv, const float* u, const float* xz, int di, float* hs, __nv_bfloat16* yhl,
                         long long plane, int B, int T, cudaStream_t st) {
   if (T == 1 && di <= 1024 && (ld * 4) % 16 == 0) {
-    const size_t stage = (size_t)16 * di * 4 + 2 * (size_t)di * 4 + (((size_t)ld * 4 + 15) & ~size_t(15));
+    // channel slices of at most 256 (a divisor of di): several small
+    // pipelines per SM keep more state bytes in flight than one wide one
+    const int W = scan_slice_width(di);
+    const size_t stage = (size_t)16 * W * 4 + 2 * (size_t)W * 4 + (((size_t)ld * 4 + 15) & ~size_t(15));
     const size_t sm = kScanStages * stage + kScanStages * 8;
     int dev = 0, n_sm = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
-    const int per_sm = (int)std::max<size_t>(1, (size_t)(220 * 1024) / sm);
-    const int grid = std::min(B, n_sm * per_sm);
+    const int per_sm = (int)std::max<size_t>(1, std::min<size_t>((size_t)(220 * 1024) / sm, 2048 / W));
+    const long long items = (long long)B * (di / W);
+    const int grid = (int)std::min<long long>(items, (long long)n_sm * per_sm);
     switch (r) {
 #define BOA_STEP_CASE(RR)                                                                                          \
   case RR:                                                                                                         \
-    scan_step_kernel<RR><<<grid, di, sm, st>>>(delta, ld, dtw, dtb, negA, Dv, u, xz, di, hs, yhl, plane, B);       \
+    scan_step_kernel<RR><<<grid, W, sm, st>>>(delta, ld, dtw, dtb, negA, Dv, u, xz, di, hs, yhl, plane, B);        \
     break;
       BOA_STEP_CASE(4)
       BOA_STEP_CASE(8)
@@ -411,13 +455,14 @@ cudaError_t launch_scan(const float* delta, int ld, int r, const float* dtw, con
     }
     return cudaGetLastError();
   }
+  const int W = scan_slice_width(di);
   dim3 block(128), grid(B, (di + 127) / 128);
   const size_t sm = (size_t)T * ld * sizeof(float);
   if (sm > 200 * 1024 || (T * ld) % 4) return cudaErrorInvalidValue;
   switch (r) {
 #define BOA_SCAN_CASE(RR)                                                                                                \
   case RR:                                                                                                               \
-    scan_tile_kernel<RR><<<grid, block, sm, st>>>(delta, ld, dtw, dtb, negA, Dv, u, xz, di, hs, yhl, plane, T);         \
+    scan_tile_kernel<RR><<<grid, block, sm, st>>>(delta, ld, dtw, dtb, negA, Dv, u, xz, di, hs, yhl, plane, T, W);      \
     break;
     BOA_SCAN_CASE(4)
     BOA_SCAN_CASE(8)

@@ -118,6 +118,7 @@ __device__ __forceinline__ void bulk_store(void* gdst, const void* smem_src, uin
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // make this thread's generic-proxy shared-memory writes visible to the async proxy
 __device__ __forceinline__ void fence_proxy_async_smem() {
