@@ -364,6 +364,35 @@ def test_cli_roundtrip(boa, weights, tmp_path):
     assert dec.read_bytes() == data
 
 
+def test_cli_multi_gpu_roundtrip(boa, weights, tmp_path):
+    """--gpus N over every GPU of the node (contiguous chunk ranges, one
+    handle and host thread per GPU): the container equals the one-GPU
+    container byte for byte and decodes on N GPUs and on one.  Needs two or
+    more GPUs; a one-GPU box skips it."""
+    import torch
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs two or more GPUs")
+    data = boa.synth.particle_stream(60000, 17)
+    src = tmp_path / "in.bin"
+    src.write_bytes(data)
+    w = weights("mamba", 64, 2, 3)
+    outs = {}
+    for g in (1, n):
+        enc = tmp_path / f"x{g}.boa"
+        r = subprocess.run([boa.CLI_PATH, "compress", w, str(src), str(enc), "64", "2", "--chunk-size", "2500",
+                            "--gpus", str(g)], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+        outs[g] = enc.read_bytes()
+    assert outs[1] == outs[n]
+    for g in (1, n):
+        dec = tmp_path / f"o{g}.bin"
+        r = subprocess.run([boa.CLI_PATH, "decompress", w, str(tmp_path / f"x{n}.boa"), str(dec), "64", "2",
+                            "--gpus", str(g)], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+        assert dec.read_bytes() == data
+
+
 def test_cli_rnn_backbone_roundtrip(boa, weights, tmp_path):
     data = boa.synth.particle_stream(5000, 8)
     src, enc, dec = tmp_path / "in.bin", tmp_path / "x.boa", tmp_path / "out.bin"
