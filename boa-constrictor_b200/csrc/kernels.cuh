@@ -20,6 +20,11 @@ struct TokenSrc {
                           //         S * chunk_len for interleaved warm-start lanes)
   const long long* lane_base;  // mode 2: byte offset of each lane's chunk in `bytes`
   const int* lane_len;         // mode 2: length of each lane's chunk
+  // Input position of the first row since the recurrent state was reset:
+  // pos0 + (d_pos ? *d_pos : 0).  Only its value mod 3 is used (the conv
+  // state is a three-slot ring indexed by position).
+  long long pos0;
+  const int* d_pos;
 };
 
 // x[row] = E[token]; xn = split(LN(x; w, b))   (rows = M, width d)
@@ -28,9 +33,12 @@ cudaError_t launch_embed_ln(const TokenSrc& src, const float* emb, int d, float*
                             cudaStream_t st);
 
 // u = silu(causal_conv4(x)), x = xz[:, :di]; rows (b, tau) with T rows per
-// chunk; conv_state [B][3][di] holds the three previous inputs.
+// chunk, row tau being input position p0 + tau (p0 = pos0 + *d_pos).
+// conv_state [B][3][di] is a ring holding the three previous inputs: slot
+// p % 3 holds the input at position p.
 cudaError_t launch_conv(const float* xz, int di, float* conv_state, const float* conv_w, const float* conv_b,
-                        float* u, __nv_bfloat16* uhl, long long plane, int B, int T, cudaStream_t st);
+                        float* u, __nv_bfloat16* uhl, long long plane, int B, int T, long long pos0,
+                        const int* d_pos, cudaStream_t st);
 
 // selective scan with fused dt_proj + softplus + D skip + SiLU(z) gate.
 // delta [M][ld_delta] = [dt_in(r) | B(16) | C(16)]; ssm_state [B][16][di];
@@ -92,6 +100,7 @@ cudaError_t launch_dec_init(DecState* ds, const uint32_t* payload, const unsigne
                             const uint32_t* lane_size, const uint8_t* lane_first, uint8_t* out,
                             const long long* lane_base, const int* lane_len, int B, cudaStream_t st);
 cudaError_t launch_set_counter(int* d_t, int value, cudaStream_t st);
+// d_t[0] += 1 and d_t[1] += 1 (decode step and input position)
 cudaError_t launch_increment(int* d_t, cudaStream_t st);
 
 // integer-CDF coder (configs[1] style): cdf [n_steps][n_streams][257]

@@ -100,13 +100,15 @@ cudaError_t launch_embed_ln(const TokenSrc& src, const float* emb, int d, float*
 // plane (d_model is a multiple of 16, so di % 4 == 0).
 __global__ void conv4_kernel(const float* __restrict__ xz, int di, float* __restrict__ cst,
                              const float* __restrict__ cw, const float* __restrict__ cb, float* __restrict__ u,
-                             __nv_bfloat16* __restrict__ uhl, long long plane, int B, int T) {
+                             __nv_bfloat16* __restrict__ uhl, long long plane, int B, int T, int ph) {
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const int q = di / 4;
   if (idx >= (long long)B * q) return;
   const int b = (int)(idx / q), c = (int)(idx - (long long)b * q) * 4;
   float4* s = reinterpret_cast<float4*>(cst + (size_t)b * 3 * di + c);
-  float4 w0 = s[0], w1 = s[di / 4], w2 = s[di / 2];
+  // ring: the first row is position p0 (p0 % 3 = ph); slots hold p0-3, p0-2, p0-1
+  const int r0 = ph, r1 = ph == 2 ? 0 : ph + 1, r2 = ph == 0 ? 2 : ph - 1;
+  float4 w0 = s[r0 * (di / 4)], w1 = s[r1 * (di / 4)], w2 = s[r2 * (di / 4)];
   const float4* k = reinterpret_cast<const float4*>(cw) + c;
   const float4 k0 = k[0], k1 = k[1], k2 = k[2], k3 = k[3];
   const float4 bias = *reinterpret_cast<const float4*>(cb + c);
@@ -143,20 +145,28 @@ __global__ void conv4_kernel(const float* __restrict__ xz, int di, float* __rest
 #pragma unroll
     for (int i = 0; i < PB; ++i) cx[i] = nx[i];
   }
-  s[0] = w0; s[di / 4] = w1; s[di / 2] = w2;
+  // after positions p0 .. p0+T-1 the window holds pn-3, pn-2, pn-1 (pn = p0 + T)
+  const int pn = (ph + T) % 3;
+  const int q0 = pn, q1 = pn == 2 ? 0 : pn + 1, q2 = pn == 0 ? 2 : pn - 1;
+  s[q0 * (di / 4)] = w0; s[q1 * (di / 4)] = w1; s[q2 * (di / 4)] = w2;
 }
 
 // Decompress step (T = 1): one thread per (chunk, 4 channels), 128-bit
 // accesses; the same conv_tap arithmetic as conv4_kernel.
 __global__ void conv_step4_kernel(const float* __restrict__ xz, int di, float* __restrict__ cst,
                                   const float* __restrict__ cw, const float* __restrict__ cb, float* __restrict__ u,
-                                  __nv_bfloat16* __restrict__ uhl, long long plane, int B) {
+                                  __nv_bfloat16* __restrict__ uhl, long long plane, int B, int ph0,
+                                  const int* __restrict__ d_pos) {
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const int q = di / 4;
   if (idx >= (long long)B * q) return;
   const int b = (int)(idx / q), c = (int)(idx - (long long)b * q) * 4;
   float4* s = reinterpret_cast<float4*>(cst + (size_t)b * 3 * di + c);
-  const float4 s0 = s[0], s1 = s[di / 4], s2 = s[di / 2];
+  // ring slot p % 3 holds position p; this step is position p, so the slots
+  // hold p-3 (oldest, slot ph), p-2 and p-1, and only slot ph is rewritten
+  int ph = (ph0 + (d_pos ? *d_pos % 3 : 0)) % 3;
+  const int r1 = ph == 2 ? 0 : ph + 1, r2 = ph == 0 ? 2 : ph - 1;
+  const float4 s0 = s[ph * (di / 4)], s1 = s[r1 * (di / 4)], s2 = s[r2 * (di / 4)];
   const float4 x = *reinterpret_cast<const float4*>(xz + (size_t)b * 2 * di + c);
   const float4 bias = *reinterpret_cast<const float4*>(cb + c);
   const float4* k = reinterpret_cast<const float4*>(cw) + c;
@@ -170,19 +180,23 @@ __global__ void conv_step4_kernel(const float* __restrict__ xz, int di, float* _
   split_bf16(o.x, h[0], l[0]); split_bf16(o.y, h[1], l[1]); split_bf16(o.z, h[2], l[2]); split_bf16(o.w, h[3], l[3]);
   *reinterpret_cast<uint2*>(uhl + (size_t)b * di + c) = *reinterpret_cast<uint2*>(h);
   *reinterpret_cast<uint2*>(uhl + plane + (size_t)b * di + c) = *reinterpret_cast<uint2*>(l);
-  s[0] = s1; s[di / 4] = s2; s[di / 2] = x;
+  s[ph * (di / 4)] = x;
 }
 
 cudaError_t launch_conv(const float* xz, int di, float* cst, const float* cw, const float* cb, float* u,
-                        __nv_bfloat16* uhl, long long plane, int B, int T, cudaStream_t st) {
-  if (di % 4 != 0) return cudaErrorInvalidValue;
+                        __nv_bfloat16* uhl, long long plane, int B, int T, long long pos0, const int* d_pos,
+                        cudaStream_t st) {
+  if (di % 4 != 0 || pos0 < 0) return cudaErrorInvalidValue;
+  const int ph0 = (int)(pos0 % 3);
   if (T == 1) {
     const long long n4 = (long long)B * (di / 4);
-    conv_step4_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(xz, di, cst, cw, cb, u, uhl, plane, B);
+    conv_step4_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(xz, di, cst, cw, cb, u, uhl, plane, B, ph0,
+                                                                    d_pos);
     return cudaGetLastError();
   }
+  if (d_pos) return cudaErrorInvalidValue;  // tiles take their position from the host
   const long long n4 = (long long)B * (di / 4);
-  conv4_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(xz, di, cst, cw, cb, u, uhl, plane, B, T);
+  conv4_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(xz, di, cst, cw, cb, u, uhl, plane, B, T, ph0);
   return cudaGetLastError();
 }
 
@@ -770,7 +784,10 @@ cudaError_t launch_wait_selftest(uint64_t limit_ns, int* ok) {
 }
 
 __global__ void set_counter_kernel(int* d_t, int v) { *d_t = v; }
-__global__ void increment_kernel(int* d_t) { *d_t += 1; }
+__global__ void increment_kernel(int* d_t) {
+  d_t[0] += 1;
+  d_t[1] += 1;
+}
 cudaError_t launch_set_counter(int* d_t, int v, cudaStream_t st) {
   set_counter_kernel<<<1, 1, 0, st>>>(d_t, v);
   return cudaGetLastError();

@@ -369,7 +369,8 @@ int forward(boa_model* m, const boa::TokenSrc& src, int B, int T, int head_mode,
       float* sst = m->ssm_st + (size_t)l * m->chunks_cap * 16 * di;
       a.N = 2 * di; a.K = d; a.bias = w.in_b; a.out_f32 = m->xz; a.ld_f32 = 2 * di;
       BOA_LAUNCH(PC_IN_PROJ, boa::gemm_launch(boa::EPI_F32, m->xn, xn_plane, 0, w.in.p, w.in.plane, a, st));
-      BOA_LAUNCH(PC_CONV, boa::launch_conv(m->xz, di, cst, w.conv_w, w.conv_b, m->u, m->uhl, u_plane, B, T, st));
+      BOA_LAUNCH(PC_CONV, boa::launch_conv(m->xz, di, cst, w.conv_w, w.conv_b, m->u, m->uhl, u_plane, B, T, src.pos0,
+                                           src.d_pos, st));
       a = boa::GemmArgs{}; a.M = M;
       a.N = m->xpN; a.K = di; a.out_f32 = m->delta; a.ld_f32 = m->xpN;
       BOA_LAUNCH(PC_X_PROJ, boa::gemm_launch(boa::EPI_F32, m->uhl, u_plane, 0, w.xp.p, w.xp.plane, a, st));
@@ -506,7 +507,9 @@ int compress_interleaved(boa_model* m, const uint8_t* d_data, uint64_t n, uint32
     // shortened instead of padded
     for (int t0 = 0; t0 < (int)chunk_len; t0 += T) {
       const int Tt = std::min<int>(T, (int)chunk_len - t0);
-      boa::TokenSrc src{1, data, rem, (int)chunk_len, t0, Tt, nullptr, stride, nullptr, nullptr};
+      // lanes carry their state from chunk to chunk: positions continue at iter * chunk_len
+      boa::TokenSrc src{1, data, rem, (int)chunk_len, t0, Tt, nullptr, stride, nullptr, nullptr,
+                        (long long)iter * chunk_len + t0, nullptr};
       boa::GemmArgs h{};
       h.tokens = data; h.n_bytes = rem; h.chunk_len = (int)chunk_len; h.stride = stride; h.t0 = t0; h.T = Tt;
       h.lf = m->lf;
@@ -828,7 +831,7 @@ int boa_compress_device(boa_model* m, const uint8_t* d_data, uint64_t n, uint32_
     BOA_LAUNCH(PC_OTHER, boa::launch_first_bytes(data, rem, chunk_len, 0, d_first + c0, Bb, st));
     const int max_len = (int)std::min<long long>(chunk_len, rem);
     for (int t0 = 0; t0 < max_len - 1; t0 += T) {
-      boa::TokenSrc src{1, data, rem, (int)chunk_len, t0, T, nullptr};
+      boa::TokenSrc src{1, data, rem, (int)chunk_len, t0, T, nullptr, 0, nullptr, nullptr, t0, nullptr};
       boa::GemmArgs h{};
       h.tokens = data; h.n_bytes = rem; h.chunk_len = (int)chunk_len; h.t0 = t0; h.T = T; h.lf = m->lf;
       if (int rc = forward(m, src, Bb, T, boa::EPI_HEAD_ENC, h)) return rc;
@@ -888,9 +891,12 @@ int boa_decompress_device(boa_model* m, const uint32_t* d_payload, const uint64_
     BOA_LAUNCH(PC_OTHER, boa::launch_dec_init(m->ds, d_payload, m->lane_off, m->lane_size, m->lane_first, d_out,
                                               m->lane_base, m->lane_len, cur, st));
     BOA_LAUNCH(PC_OTHER, boa::launch_set_counter(m->d_t, 1, st));
+    // input position of step 1 (d_t[1], advanced with d_t[0]): warm-start lanes
+    // continue from the previous chunk, at it * chunk_len
+    BOA_LAUNCH(PC_OTHER, boa::launch_set_counter(m->d_t + 1, m->warm ? (int)(((long long)it * chunk_len) % 3) : 0, st));
     const int max_len = (int)std::min<long long>(chunk_len, (long long)n - (long long)c0 * chunk_len);
     if (max_len <= 1 && !m->warm) continue;
-    boa::TokenSrc src{2, d_out, (long long)n, (int)chunk_len, 0, 1, m->d_t, 0, m->lane_base, m->lane_len};
+    boa::TokenSrc src{2, d_out, (long long)n, (int)chunk_len, 0, 1, m->d_t, 0, m->lane_base, m->lane_len, 0, m->d_t + 1};
     boa::GemmArgs h{};
     h.out_bytes = d_out; h.n_bytes = (long long)n; h.chunk_len = (int)chunk_len; h.d_t = m->d_t; h.dstates = m->ds;
     h.payload = d_payload; h.offsets = m->lane_off; h.lane_base = m->lane_base; h.lane_len = m->lane_len;
@@ -1060,7 +1066,7 @@ int boa_model_logits(boa_model* m, const uint8_t* tokens, int B, int L, int mode
   if (mode == 0) {
     for (int t0 = 0; t0 < L; t0 += T) {
       const int Tt = std::min(T, L - t0);
-      boa::TokenSrc src{1, d_tok, (long long)B * L, L, t0, Tt, nullptr, (long long)L, nullptr, nullptr};
+      boa::TokenSrc src{1, d_tok, (long long)B * L, L, t0, Tt, nullptr, (long long)L, nullptr, nullptr, t0, nullptr};
       boa::GemmArgs h{};
       h.out_f32 = d_lg; h.ld_f32 = 256;
       if (int rc = forward(m, src, B, Tt, boa::EPI_LOGITS, h)) return rc;
@@ -1076,7 +1082,7 @@ int boa_model_logits(boa_model* m, const uint8_t* tokens, int B, int L, int mode
     for (int t = 0; t < L; ++t) {
       for (int b = 0; b < B; ++b) col[b] = tokens[(size_t)b * L + t];
       BOA_CK(cudaMemcpyAsync(d_col, col.data(), B, cudaMemcpyHostToDevice, st));
-      boa::TokenSrc src{0, d_col, 0, 0, 0, 1, nullptr};
+      boa::TokenSrc src{0, d_col, 0, 0, 0, 1, nullptr, 0, nullptr, nullptr, t, nullptr};
       boa::GemmArgs h{};
       h.out_f32 = d_lg; h.ld_f32 = 256;
       if (int rc = forward(m, src, B, 1, boa::EPI_LOGITS, h)) return rc;
