@@ -9,12 +9,17 @@
 // path can be written or read with this coder in place of the reference's.
 //
 // The reference runs one thread per stream, builds all K+1 CDF entries in a
-// 1025-entry local array and reads its row with strided scalar loads.  Here a
-// warp stages the rows of 32 streams through shared memory with coalesced
-// loads and each lane runs its own row's fp64 prefix sum (whose rounding fixes
-// the CDF).  The encoder needs only P_s, P_s+1 and P_K, so it reads the row
-// once and builds no table; the decoder records P at every 64-entry slab
-// start, picks the one slab holding its target and re-reads only that slab.
+// 1025-entry local array and reads its row with strided scalar loads.  Here
+// one lane still owns one stream, but a warp stages the rows of its 32
+// streams through shared memory, and each lane runs its own row's fp64 prefix
+// sum (whose rounding fixes the CDF).  The encoder needs only P_s, P_s+1 and
+// P_K, so it reads the row once and builds no table.  Two staging forms:
+//   - K <= 256 with K % 4 == 0 (the codec's K = 256): the warp's 32 rows land
+//     in shared memory by one bulk async copy per row; the decoder records P
+//     at every 16th entry, binary-searches those marks and scans 16 entries;
+//   - any other K (up to 1024): 64-column slabs staged with coalesced loads;
+//     the decoder records P at every slab start, picks the slab holding its
+//     target and re-reads only that slab.
 #include <string>
 
 #include "kernels.cuh"
