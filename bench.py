@@ -3,19 +3,27 @@
 Workload: the 256-d / 8-layer Mamba predictor,
 random-init weights (seed 0), over a 256 MiB stream of seeded synthetic
 float32 particle records (seed 1 + rank) split into 16,384 chunks of 16 KiB,
-all chunks in one batch.  One step = compress the whole stream on the GPU and
-decompress it again (a byte-exact round trip, verified after timing).
+all chunks in one batch.  One step = one 64-position compress tile plus the 64
+decode steps of the same positions, over every chunk: the K timed steps are
+one compress call over the chunks' first 64K + 1 bytes and one decompress call
+(256 steps are the whole chunks).  The round trip is verified after timing; a
+mismatch exits with status 3.
 
   python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference]
-  python bench.py --workload pyrc   # the Python codec's batch coder (secondary line)
-  python bench.py --workload cms    # the reference's cms_experiment model (mambav1
-                                    # d64 L2, its trained weights) on 16,384 chunks
-                                    # of 4 KiB: the configuration of the reference's
-                                    # published MB/s, so vs_baseline is set
+  python bench.py --workload coder     # configs[1]: the integer range coder alone
+  python bench.py --workload configs3  # minGRU d256 L8 on the order-2 Markov source
+  python bench.py --workload configs4  # Mamba d512 L16, 262,144 chunks split over the GPUs
+  python bench.py --workload cms       # the reference's cms_experiment model (mambav1
+                                       # d64 L2, its trained weights) on 16,384 chunks
+                                       # of 4 KiB: the configuration of the reference's
+                                       # published MB/s, so vs_baseline is set
+  python bench.py --workload pyrc      # the Python codec's batch coder
 
-Under torchrun each rank drives its own GPU with its own 256 MiB shard (weak
-scaling; chunks are independent so no collective touches the data path; the
-only cross-rank traffic is the barrier and the max-reduction of the timings).
+Under torchrun each rank drives its own GPU.  configs[2]: every rank codes its
+own 256 MiB stream (weak scaling); configs[4]: the workload's chunks are split
+over the ranks (strong scaling).  Chunks are independent, so no collective
+touches the data path; the only cross-rank traffic is the barrier and the
+max-reduction of the timings.
 
 value  = MB/s (2^20 B) of input round-tripped per second, whole job, inputs
          resident in HBM, device time (CUDA events) max over ranks.
@@ -142,10 +150,10 @@ def step_roofline(d, L, B, T, hbm_gbs, tf_sust):
             "weight_bytes": weight_bytes}
 
 
-# DRAM bytes (read + write) of one launch from `ncu --set full` (the
-# small-round-trip capture summarised under profiles/), per chunk of the batch (the
-# kernel's traffic scales with the number of chunks): decompress-step scan.
-NCU_TRAFFIC_PER_CHUNK = {("scan", "decode"): (609.040384e6 + 524.623360e6) / 16384}
+# DRAM bytes (read + write) of one launch from `ncu --set full` (the capture
+# summarised in profiles/ncu_configs2_step_kernels.md), per chunk of the batch
+# (the kernel's traffic scales with the number of chunks): decompress-step scan.
+NCU_TRAFFIC_PER_CHUNK = {("scan", "decode"): (607.283e6 + 512.869e6) / 16384}
 
 
 # --------------------------------------------------------------------------- clocks
