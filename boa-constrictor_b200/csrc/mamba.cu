@@ -845,69 +845,77 @@ cudaError_t launch_rc_encode_cdf(EncState* es, const uint32_t* cdf, const uint8_
   return cudaGetLastError();
 }
 
-// Decoder: one warp per stream.  Lane l holds Q[l + 32k] (k = 0..7), so each
-// of the eight loads of a row is one coalesced 128-byte access, and the next
-// step's row is loaded before the current step's search so the two overlap.
-// Search: the decoded symbol is the s with Q[s] <= target < Q[s+1]
-// (range_coder_kernels.cu:743-763).  For a non-decreasing CDF the entries
-// <= target are exactly Q[0..s], so every lane counts its entries <= target
-// and one warp reduction gives s + 1; Q[256] = 2^24 exceeds every target.
-// (The reference's lowest-match rule agrees with this on every
-// non-decreasing CDF, which includes every CDF the encoder can code.)  A
-// count of 0 (Q[0] > target) decodes symbol 0 with an empty interval, as the
-// reference's no-match path does.  The coder state is warp-uniform.
-__device__ __forceinline__ void dec_row_load(const uint32_t* __restrict__ q, int lane, uint32_t (&v)[8]) {
+// Decoder: two streams per warp, one per 16-lane half.  Lane l of a half
+// holds Q[l + 16k] (k = 0..15), so each of a row's sixteen loads is one
+// 64-byte segment per stream, and the next step's row is loaded before the
+// current step's search so the two overlap.  Search: the decoded symbol is
+// the s with Q[s] <= target < Q[s+1] (range_coder_kernels.cu:743-763).  For a
+// non-decreasing CDF the entries <= target are exactly Q[0..s], so every
+// lane counts its entries <= target; one warp reduction sums both halves at
+// once (half 1's count shifted into the upper 16 bits) and gives s + 1;
+// Q[256] = 2^24 exceeds every target.  (The reference's lowest-match rule
+// agrees with this on every non-decreasing CDF, which includes every CDF the
+// encoder can code.)  A count of 0 (Q[0] > target) decodes symbol 0 with an
+// empty interval, as the reference's no-match path does.  The coder state is
+// uniform within a half, so the scalar coder arithmetic is shared by two
+// streams' worth of lanes instead of one.
+__device__ __forceinline__ void dec_row_load(const uint32_t* __restrict__ q, int hl, uint32_t (&v)[16]) {
 #pragma unroll
-  for (int k = 0; k < 8; ++k) v[k] = __ldcs(q + lane + 32 * k);
+  for (int k = 0; k < 16; ++k) v[k] = __ldcs(q + hl + 16 * k);
 }
 __global__ void __launch_bounds__(256) rc_decode_cdf_kernel(DecState* ds, const uint32_t* __restrict__ cdf,
                                                             const uint32_t* __restrict__ payload,
                                                             const unsigned long long* __restrict__ off, int n_streams,
                                                             int n_steps, uint8_t* __restrict__ syms) {
-  const int i = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (i >= n_streams) return;
-  DecState s = ds[i];
-  const uint32_t* in = payload + off[i];
-  uint32_t v[8];
-  dec_row_load(cdf + (size_t)i * 257, lane, v);
+  const int half = (threadIdx.x >> 4) & 1, hl = threadIdx.x & 15;
+  const int i = (blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5)) * 2 + half;
+  if (i - half >= n_streams) return;        // whole warp past the end
+  const bool live = i < n_streams;          // an odd last stream leaves half 1 idle (it still joins the warp ops)
+  const int ii = live ? i : i - 1;          // idle half mirrors half 0's reads
+  DecState s = ds[ii];
+  const uint32_t* in = payload + off[ii];
+  uint32_t v[16];
+  dec_row_load(cdf + (size_t)ii * 257, hl, v);
   for (int t = 0; t < n_steps; ++t) {
-    const size_t rowi = (size_t)t * n_streams + i;
-    uint32_t nv[8];
-    if (t + 1 < n_steps) dec_row_load(cdf + (rowi + n_streams) * 257, lane, nv);
+    const size_t rowi = (size_t)t * n_streams + ii;
+    uint32_t nv[16];
+    if (t + 1 < n_steps) dec_row_load(cdf + (rowi + n_streams) * 257, hl, nv);
     const uint32_t target = dec_target(s);
     unsigned cnt = 0;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) cnt += v[k] <= target ? 1u : 0u;
-    const int c = (int)__reduce_add_sync(0xffffffffu, cnt);
+    for (int k = 0; k < 16; ++k) cnt += v[k] <= target ? 1u : 0u;
+    const unsigned both = __reduce_add_sync(0xffffffffu, cnt << (16 * half));
+    const int c = (int)((both >> (16 * half)) & 0xffffu);
     int sym = 0;
     uint32_t lo = 0, hi = 0;
-    if (c > 0) {
-      sym = c - 1;
-      const int k = sym >> 5, kn = (sym + 1) >> 5;
-      uint32_t a = v[0], b = v[0];
+    const int sk = c > 0 ? c - 1 : 0, k = sk >> 4, kn = (sk + 1) >> 4;
+    uint32_t a = v[0], b = v[0];
 #pragma unroll
-      for (int j = 1; j < 8; ++j) {  // warp-uniform register selects, no local memory
-        if (j == k) a = v[j];
-        if (j == kn) b = v[j];
-      }
-      lo = __shfl_sync(0xffffffffu, a, sym & 31);
-      hi = __shfl_sync(0xffffffffu, b, (sym + 1) & 31);
-      if (sym == 255) hi = __ldg(cdf + rowi * 257 + 256);
+    for (int j = 1; j < 16; ++j) {  // register selects, no local memory
+      if (j == k) a = v[j];
+      if (j == kn) b = v[j];
     }
-    if (lane == 0) syms[rowi] = (uint8_t)sym;
+    const uint32_t la = __shfl_sync(0xffffffffu, a, half * 16 + (sk & 15));
+    const uint32_t lb = __shfl_sync(0xffffffffu, b, half * 16 + ((sk + 1) & 15));
+    if (c > 0) {
+      sym = sk;
+      lo = la;
+      hi = sym == 255 ? __ldg(cdf + rowi * 257 + 256) : lb;
+    }
+    if (hl == 0 && live) syms[rowi] = (uint8_t)sym;
     dec_update(s, lo, hi, in);
     if (t + 1 < n_steps) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = nv[k];
+      for (int q = 0; q < 16; ++q) v[q] = nv[q];
     }
   }
-  if (lane == 0) ds[i] = s;
+  if (hl == 0 && live) ds[i] = s;
 }
 cudaError_t launch_rc_decode_cdf(DecState* ds, const uint32_t* cdf, const uint32_t* payload,
                                  const unsigned long long* off, int n_streams, int n_steps, uint8_t* syms,
                                  cudaStream_t st) {
-  rc_decode_cdf_kernel<<<(n_streams + 7) / 8, 256, 0, st>>>(ds, cdf, payload, off, n_streams, n_steps, syms);
+  const int warps = (n_streams + 1) / 2;
+  rc_decode_cdf_kernel<<<(warps + 7) / 8, 256, 0, st>>>(ds, cdf, payload, off, n_streams, n_steps, syms);
   return cudaGetLastError();
 }
 
