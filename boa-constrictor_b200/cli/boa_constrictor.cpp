@@ -149,17 +149,32 @@ int do_decompress(const Opts& o) {
   const uint32_t n = I.n_chunks;
   std::vector<uint8_t> first(n);
   std::vector<uint64_t> off(n), len(n);
-  boa_boa2_parse(buf.data(), buf.size(), &I, first.data(), off.data(), len.data());
+  if (boa_boa2_parse(buf.data(), buf.size(), &I, first.data(), off.data(), len.data())) {
+    std::cerr << "Error: not a valid BOA2 container\n";
+    return 1;
+  }
   std::vector<uint32_t> sizes(n), lens(n, I.chunk_len);
   if (n) lens[n - 1] = I.last_chunk_len;
   std::vector<uint32_t> words;
+  uint64_t stream_total = 0;
   for (uint32_t i = 0; i < n; ++i) {
+    // every stream must lie inside the file and the payload must add up
+    if (I.payload_offset > buf.size() || off[i] > buf.size() - I.payload_offset ||
+        len[i] > buf.size() - I.payload_offset - off[i]) {
+      std::cerr << "Error: stream " << i << " lies outside the container\n";
+      return 1;
+    }
+    stream_total += len[i];
     if (len[i] % 4) { std::cerr << "Error: stream " << i << " is not a whole number of words\n"; return 1; }
     sizes[i] = (uint32_t)(len[i] / 4);
     const uint8_t* p = buf.data() + I.payload_offset + off[i];
     const size_t w0 = words.size();
     words.resize(w0 + sizes[i]);
     std::memcpy(words.data() + w0, p, len[i]);
+  }
+  if (stream_total > I.payload_bytes) {
+    std::cerr << "Error: stream lengths exceed the payload\n";
+    return 1;
   }
   std::vector<uint64_t> woff(n + 1, 0);
   for (uint32_t i = 0; i < n; ++i) woff[i + 1] = woff[i] + sizes[i];

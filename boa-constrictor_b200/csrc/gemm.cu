@@ -397,7 +397,12 @@ struct PCfg {
   static constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;
   static constexpr int kEpiBuf = kEpiWarps * 32 * kTileStride * 4;  // staging tiles
   static constexpr int kRed = kBM * 4 * 2 * 4;
-  static constexpr int kPrm = (kMaxPersistN + 2 * 512) * 4;  // bias [N], ln_w / ln_b [BN <= 512]
+  // bias [N] and ln_w / ln_b [BN].  Narrow tiles (BN < 128) only serve N <= 512
+  // (pick_bn: d_model 80's in_proj, N = 320, is the widest), so their staging
+  // is small and the room goes to a fourth stage at BN = 48 (x_proj).
+  static constexpr int kBiasN = BN < 128 ? 512 : kMaxPersistN;
+  static constexpr int kLnN = BN < 128 ? 128 : 512;
+  static constexpr int kPrm = (kBiasN + 2 * kLnN) * 4;
   static constexpr int kBudget = 225 * 1024 - 1024 - 256 - kRed - kEpiBuf - kPrm;
   static constexpr int kStages = kBudget / kStageBytes > 8 ? 8 : kBudget / kStageBytes;
   // N > 256 (LayerNorm over d = 512): 256-wide MMAs side by side in one
@@ -430,8 +435,8 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* red = reinterpret_cast<float*>(smem + Cfg::kStages * Cfg::kStageBytes + Cfg::kEpiBuf + 256);  // [128][4][2]
   float* prm = red + kBM * 4 * 2;  // bias [N] | ln_w [BN] | ln_b [BN]
-  float* prm_w = prm + kMaxPersistN;
-  float* prm_b = prm_w + 512;
+  float* prm_w = prm + Cfg::kBiasN;
+  float* prm_b = prm_w + Cfg::kLnN;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles_n = args.N / BN;
@@ -929,6 +934,7 @@ cudaError_t gemm_launch(int mode, const __nv_bfloat16* A, long long a_plane, int
                         const __nv_bfloat16* W, long long w_plane, const GemmArgs& args, cudaStream_t stream) {
   if (args.K % 16 != 0 || args.K <= 0 || args.M <= 0) return cudaErrorInvalidValue;
   if (mode <= EPI_RES_LN && args.N > kMaxPersistN) return cudaErrorInvalidValue;  // bias staging size
+  if (mode <= EPI_RES_LN && pick_bn(mode, args.N) < 128 && args.N > 512) return cudaErrorInvalidValue;
   const int BN = pick_bn(mode, args.N);
   if (BN != 48 && BN != 64 && BN != 80 && BN != 128 && BN != 160 && BN != 256 && BN != 512)
     return cudaErrorInvalidValue;

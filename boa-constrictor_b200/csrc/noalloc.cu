@@ -21,7 +21,10 @@ constexpr int kNoAllocMaxStreams = 65536;  // 65536 x 32 B = 2 MiB per GPU, held
 static __device__ __align__(256) EncState g_noalloc_states[kNoAllocMaxStreams];
 
 // Device address of g_noalloc_states on the current device, looked up once
-// per device (with that device current) and cached.
+// per device (with that device current) and cached for the life of the
+// process.  A caller that destroys its primary context (cudaDeviceReset)
+// invalidates the cached address, so such a caller must not use this entry
+// point afterwards.
 static EncState* noalloc_scratch(cudaError_t* err) {
   static std::mutex mu;
   static EncState* addr[64] = {nullptr};
@@ -52,6 +55,14 @@ extern "C" int boa_rc_encode_cdf_noalloc(const uint32_t* d_cdf, const uint8_t* d
     return fail(nullptr, BOA_E_INVALID,
                 "boa_rc_encode_cdf_noalloc: pitch_words below boa_stream_capacity_words(n_steps + 1)");
   cudaError_t e;
+  if (stream) {  // the states live on the current device: the stream must belong to it
+    int cur = -1, sdev = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess || cudaStreamGetDevice((cudaStream_t)stream, &sdev) != cudaSuccess ||
+        cur != sdev) {
+      cudaGetLastError();
+      return fail(nullptr, BOA_E_INVALID, "boa_rc_encode_cdf_noalloc: the stream belongs to another device");
+    }
+  }
   boa::EncState* es = boa::noalloc_scratch(&e);
   if (!es) return fail(nullptr, BOA_E_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
   cudaStream_t st = (cudaStream_t)stream;

@@ -188,9 +188,11 @@ int boa_rc_decode_cdf(boa_model* h, const uint32_t* cdf, int n_streams, int n_st
  * and its word count to d_sizes[i].  The per-stream coder states live in one
  * static device array of 65536 x 32 bytes (2 MiB), held by every GPU that
  * loads the library until exit; n_streams above 65536 is rejected.  Work is
- * enqueued on `stream` (NULL = legacy default stream) and nothing is
- * synchronised.  The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress), so make it before any stream capture.
+ * enqueued on `stream` (NULL = legacy default stream), which must belong to
+ * the current device (BOA_E_INVALID otherwise), and nothing is synchronised.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress), so make it before any stream capture; the
+ * address is kept for the life of the process, so do not call this after a
+ * cudaDeviceReset of that device.
  * Every call shares the array and resets the states it uses: calls that
  * overlap on the GPU race.  Argument and launch errors are returned (message
  * in boa_last_error(NULL)).  A stream whose coding stopped on the device (an

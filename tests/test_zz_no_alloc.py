@@ -131,3 +131,17 @@ def test_noalloc_encoder_rejects_oversize(boa):
     rc = L.boa_rc_encode_cdf_noalloc(one, one, 65537, 10, one, boa.capacity_words(11), one, None)
     assert rc == boa.BOA_E_INVALID
     assert b"maximum" in L.boa_last_error(None)
+
+
+def test_noalloc_rejects_a_stream_of_another_device(boa):
+    """The coder states live on the current device; a stream created on
+    another GPU is an argument error, not a launch failure.  Needs two GPUs."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two or more GPUs")
+    other = torch.cuda.Stream(device=1)
+    torch.cuda.set_device(0)
+    one = C.c_void_p(16)  # never dereferenced: the stream check comes first
+    rc = boa.lib().boa_rc_encode_cdf_noalloc(one, one, 4, 10, one, boa.capacity_words(11), one,
+                                             C.c_void_p(other.cuda_stream))
+    assert rc == boa.BOA_E_INVALID and b"another device" in boa.lib().boa_last_error(None)
