@@ -758,7 +758,9 @@ int boa_set_batch(boa_model* m, int chunks, int tile) {
 }
 
 int boa_batch_geometry(boa_model* m, uint32_t n_chunks, uint32_t chunk_len, int compress, int* chunks, int* tile) {
-  if (!m || !chunks || !tile || n_chunks == 0 || chunk_len == 0) return BOA_E_INVALID;
+  if (!m) return BOA_E_INVALID;
+  if (!chunks || !tile || n_chunks == 0 || chunk_len == 0)
+    return fail(m, BOA_E_INVALID, "boa_batch_geometry: null output or empty geometry");
   DeviceGuard dev(m->device);
   int B, T;
   if (m->warm) {

@@ -407,6 +407,23 @@ def test_cli_rnn_backbone_roundtrip(boa, weights, tmp_path):
     assert dec.read_bytes() == data
 
 
+def test_batch_geometry_reports_the_run(boa, m64):
+    """boa_batch_geometry reports the batch a call would use: every chunk in
+    one batch when they fit, the configured batch and tile when set, one
+    position per decode step, and the tile clipped to the chunk."""
+    assert m64.batch_geometry(100, 4096, True) == (100, 64)
+    assert m64.batch_geometry(100, 4096, False) == (100, 1)
+    assert m64.batch_geometry(100, 10, True) == (100, 9)
+    m64.set_batch(7, 32)
+    try:
+        assert m64.batch_geometry(100, 4096, True) == (7, 32)
+        assert m64.batch_geometry(5, 4096, False) == (5, 1)
+    finally:
+        m64.set_batch(0, 0)
+    with pytest.raises(boa.BoaError):
+        m64.batch_geometry(0, 4096, True)
+
+
 def test_state_reset_after_a_larger_batch(boa, m64):
     """A call with fewer chunks than an earlier one must start from zero state
     in every layer."""
