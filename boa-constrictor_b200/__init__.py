@@ -70,6 +70,7 @@ SIGNATURES = {
     "boa_set_batch": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
     "boa_set_warm_start": (C.c_int, [C.c_void_p, C.c_uint32]),
     "boa_batch_geometry": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_int, _i32p, _i32p]),
+    "boa_reserve": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32]),
     "boa_stream_capacity_words": (C.c_uint32, [C.c_uint32]),
     "boa_compress_chunks": (C.c_int, [C.c_void_p, _u8p, C.c_size_t, C.c_uint32, C.c_uint32, C.c_uint32, _u8p,
                                       _u32p, C.c_size_t, _u32p, _u64p]),
@@ -181,6 +182,10 @@ class Model:
         _check(lib().boa_batch_geometry(self.h, n_chunks, chunk_len, int(bool(compress)), C.byref(b), C.byref(t)),
                self.h)
         return b.value, t.value
+
+    def reserve(self, n_chunks: int, chunk_len: int):
+        """Allocate now what calls over this geometry will need."""
+        _check(lib().boa_reserve(self.h, n_chunks, chunk_len), self.h)
 
     def set_warm_start(self, interleave_batch: int):
         _check(lib().boa_set_warm_start(self.h, interleave_batch), self.h)

@@ -774,6 +774,30 @@ int boa_batch_geometry(boa_model* m, uint32_t n_chunks, uint32_t chunk_len, int 
   return 0;
 }
 
+int boa_reserve(boa_model* m, uint32_t n_chunks, uint32_t chunk_len) {
+  if (!m) return BOA_E_INVALID;
+  if (n_chunks == 0 || chunk_len == 0) return fail(m, BOA_E_INVALID, "boa_reserve: empty geometry");
+  DeviceGuard dev(m->device);
+  int B, T;
+  if (m->warm) {
+    B = (int)std::min<uint32_t>(m->warm, n_chunks);
+    T = std::max(1, std::min<int>(m->cfg_tile > 0 ? m->cfg_tile : 64, (int)std::max<uint32_t>(1, chunk_len - 1)));
+  } else {
+    pick_batch(m, n_chunks, chunk_len, true, B, T);
+  }
+  const uint32_t pitch = boa_stream_capacity_words(chunk_len);
+  if (int rc = ensure_work(m, (size_t)B * T, B, pitch)) return rc;  // the compress form; decode needs less
+  // staging of the host-buffer calls (boa_compress_chunks / boa_decompress_chunks) for this geometry
+  auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
+  const size_t nb = (size_t)n_chunks * chunk_len, words = (size_t)n_chunks * pitch;
+  const size_t io = std::max(al(nb) + al(n_chunks) + al(words * 4) + al((size_t)n_chunks * 4) +
+                                 al(((size_t)n_chunks + 1) * 8),
+                             al(words * 4 + 4) + al((size_t)n_chunks * 4) + al(((size_t)n_chunks + 1) * 8) +
+                                 al(n_chunks) + al(nb));
+  if (!ensure_io(m, io)) return fail(m, BOA_E_NOMEM, "boa_reserve: device staging allocation failed");
+  return 0;
+}
+
 uint64_t boa_device_bytes(const boa_model* m) {
   return m ? (uint64_t)(m->wbytes + m->work_bytes + m->io_bytes) : 0;
 }

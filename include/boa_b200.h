@@ -84,6 +84,13 @@ int boa_set_batch(boa_model* h, int chunks_per_batch, int tile_tokens);
  * reports them before a run.  Allocates nothing. */
 int boa_batch_geometry(boa_model* h, uint32_t n_chunks, uint32_t chunk_len, int compress, int* chunks_per_batch,
                        int* tile_tokens);
+/* Allocates now what compress / decompress calls over n_chunks chunks of up
+ * to chunk_len bytes will need (work buffers for the batch the call would
+ * pick, and the staging of the host-buffer calls), so that those calls
+ * allocate nothing: the role of BoaPredictorGPU::allocate_chunk
+ * (boa_gpu.hpp:268-300), called before the timed loops.  Buffers only grow;
+ * a later call with a larger geometry still allocates. */
+int boa_reserve(boa_model* h, uint32_t n_chunks, uint32_t chunk_len);
 /* --warm-start (boa.cpp:313-319, :395-435, :608-610): with interleave_batch
  * W > 0 the codec runs W lanes; lane b codes chunks b*S, b*S+1, ... with
  * S = ceil(n_chunks / W), carrying the model state from chunk to chunk (each

@@ -424,6 +424,22 @@ def test_batch_geometry_reports_the_run(boa, m64):
         m64.batch_geometry(0, 4096, True)
 
 
+def test_reserve_allocates_up_front(boa, weights):
+    """After boa_reserve for a geometry, compress and decompress calls over it
+    (device and host-buffer forms) allocate nothing more: the handle's device
+    footprint stays the same."""
+    m = boa.Model(weights("mamba", 64, 2, 3), "mamba", 64, 2)
+    data = boa.synth.particle_stream(40 * 777, 19)
+    m.reserve(40, 777)
+    before = m.device_bytes()
+    assert before > 0
+    fb, sizes, pay = m.compress(data, 777)
+    assert m.decompress(fb, sizes, pay, [777] * 40, 777) == data
+    assert m.device_bytes() == before
+    with pytest.raises(boa.BoaError):
+        m.reserve(0, 777)
+
+
 def test_state_reset_after_a_larger_batch(boa, m64):
     """A call with fewer chunks than an earlier one must start from zero state
     in every layer."""
