@@ -32,20 +32,23 @@ cudaError_t launch_embed_ln(const TokenSrc& src, const float* emb, int d, float*
                             long long xn_plane, const float* ln_w, const float* ln_b, int M,
                             cudaStream_t st);
 
-// u = silu(causal_conv4(x)), x = xz[:, :di]; rows (b, tau) with T rows per
+// u = silu(causal_conv4(x)) as bf16 hi / lo planes (uhl), x = xz[:, :di]; rows (b, tau) with T rows per
 // chunk, row tau being input position p0 + tau (p0 = pos0 + *d_pos).
 // conv_state [B][3][di] is a ring holding the three previous inputs: slot
 // p % 3 holds the input at position p.
 cudaError_t launch_conv(const float* xz, int di, float* conv_state, const float* conv_w, const float* conv_b,
-                        float* u, __nv_bfloat16* uhl, long long plane, int B, int T, long long pos0,
+                        __nv_bfloat16* uhl, long long plane, int B, int T, long long pos0,
                         const int* d_pos, cudaStream_t st);
 
 // selective scan with fused dt_proj + softplus + D skip + SiLU(z) gate.
 // delta [M][ld_delta] = [dt_in(r) | B(16) | C(16)]; ssm_state [B][16][di];
-// negA holds -exp(A_log) * log2(e) per (channel, state).
+// negA holds -exp(A_log) * log2(e) per (channel, state).  u comes as the
+// conv's bf16 hi / lo planes (used as hi + lo); y * silu(z) leaves as hi / lo
+// planes in yhl, a different buffer with the same plane stride.
 cudaError_t launch_scan(const float* delta, int ld_delta, int r, const float* dt_w, const float* dt_b,
-                        const float* negA, const float* Dv, const float* u, const float* xz, int di,
-                        float* ssm_state, __nv_bfloat16* yhl, long long plane, int B, int T, cudaStream_t st);
+                        const float* negA, const float* Dv, const float* xz, int di,
+                        float* ssm_state, const __nv_bfloat16* uhl, __nv_bfloat16* yhl, long long plane, int B, int T,
+                        cudaStream_t st);
 
 cudaError_t scan_prepare_device();
 // one bounded mbarrier wait that runs out (failure-detection self-test)

@@ -99,7 +99,7 @@ cudaError_t launch_embed_ln(const TokenSrc& src, const float* emb, int d, float*
 // with 128-bit loads of x and stores of u and 64-bit stores of each bf16
 // plane (d_model is a multiple of 16, so di % 4 == 0).
 __global__ void conv4_kernel(const float* __restrict__ xz, int di, float* __restrict__ cst,
-                             const float* __restrict__ cw, const float* __restrict__ cb, float* __restrict__ u,
+                             const float* __restrict__ cw, const float* __restrict__ cb,
                              __nv_bfloat16* __restrict__ uhl, long long plane, int B, int T, int ph) {
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const int q = di / 4;
@@ -133,7 +133,6 @@ __global__ void conv4_kernel(const float* __restrict__ xz, int di, float* __rest
         o.y = conv_tap(w0.y, w1.y, w2.y, xt.y, k1, bias.y);
         o.z = conv_tap(w0.z, w1.z, w2.z, xt.z, k2, bias.z);
         o.w = conv_tap(w0.w, w1.w, w2.w, xt.w, k3, bias.w);
-        *reinterpret_cast<float4*>(u + row * di + c) = o;
         __nv_bfloat16 h[4], l[4];
         split_bf16(o.x, h[0], l[0]); split_bf16(o.y, h[1], l[1]);
         split_bf16(o.z, h[2], l[2]); split_bf16(o.w, h[3], l[3]);
@@ -154,7 +153,7 @@ __global__ void conv4_kernel(const float* __restrict__ xz, int di, float* __rest
 // Decompress step (T = 1): one thread per (chunk, 4 channels), 128-bit
 // accesses; the same conv_tap arithmetic as conv4_kernel.
 __global__ void conv_step4_kernel(const float* __restrict__ xz, int di, float* __restrict__ cst,
-                                  const float* __restrict__ cw, const float* __restrict__ cb, float* __restrict__ u,
+                                  const float* __restrict__ cw, const float* __restrict__ cb,
                                   __nv_bfloat16* __restrict__ uhl, long long plane, int B, int ph0,
                                   const int* __restrict__ d_pos) {
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -175,7 +174,6 @@ __global__ void conv_step4_kernel(const float* __restrict__ xz, int di, float* _
   o.y = conv_tap(s0.y, s1.y, s2.y, x.y, k[1], bias.y);
   o.z = conv_tap(s0.z, s1.z, s2.z, x.z, k[2], bias.z);
   o.w = conv_tap(s0.w, s1.w, s2.w, x.w, k[3], bias.w);
-  *reinterpret_cast<float4*>(u + (size_t)b * di + c) = o;
   __nv_bfloat16 h[4], l[4];
   split_bf16(o.x, h[0], l[0]); split_bf16(o.y, h[1], l[1]); split_bf16(o.z, h[2], l[2]); split_bf16(o.w, h[3], l[3]);
   *reinterpret_cast<uint2*>(uhl + (size_t)b * di + c) = *reinterpret_cast<uint2*>(h);
@@ -183,20 +181,20 @@ __global__ void conv_step4_kernel(const float* __restrict__ xz, int di, float* _
   s[ph * (di / 4)] = x;
 }
 
-cudaError_t launch_conv(const float* xz, int di, float* cst, const float* cw, const float* cb, float* u,
+cudaError_t launch_conv(const float* xz, int di, float* cst, const float* cw, const float* cb,
                         __nv_bfloat16* uhl, long long plane, int B, int T, long long pos0, const int* d_pos,
                         cudaStream_t st) {
   if (di % 4 != 0 || pos0 < 0) return cudaErrorInvalidValue;
   const int ph0 = (int)(pos0 % 3);
   if (T == 1) {
     const long long n4 = (long long)B * (di / 4);
-    conv_step4_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(xz, di, cst, cw, cb, u, uhl, plane, B, ph0,
+    conv_step4_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(xz, di, cst, cw, cb, uhl, plane, B, ph0,
                                                                     d_pos);
     return cudaGetLastError();
   }
   if (d_pos) return cudaErrorInvalidValue;  // tiles take their position from the host
   const long long n4 = (long long)B * (di / 4);
-  conv4_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(xz, di, cst, cw, cb, u, uhl, plane, B, T, ph0);
+  conv4_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(xz, di, cst, cw, cb, uhl, plane, B, T, ph0);
   return cudaGetLastError();
 }
 
@@ -251,6 +249,13 @@ __device__ __forceinline__ float scan_update(const float4* __restrict__ dl4, con
   return __fmul_rn(y, __fdividef(z, __fadd_rn(1.0f, __expf(-z))));  // y * silu(z)
 }
 
+// The scan's u input: the conv writes u only as the bf16 hi / lo planes that
+// x_proj consumes, and both scan forms use it as hi + lo (about 2^-17
+// relative to the fp32 value), with the same rounding everywhere.
+__device__ __forceinline__ float u_from_planes(__nv_bfloat16 hi, __nv_bfloat16 lo) {
+  return __fadd_rn(__bfloat162float(hi), __bfloat162float(lo));
+}
+
 // Selective-scan state layout, shared by both forms: the di channels of a
 // chunk are cut into slices of W (a divisor of di), and each (chunk, slice)
 // holds its 16 state rows of W floats contiguously, so the decode form moves
@@ -277,8 +282,8 @@ int scan_slice_width(int di) {
 template <int R, int CPT>
 __global__ void __launch_bounds__(128, CPT == 1 ? 5 : 3) scan_tile_kernel(
     const float* __restrict__ delta, int ld, const float* __restrict__ dtw, const float* __restrict__ dtb,
-    const float* __restrict__ negA, const float* __restrict__ Dv, const float* __restrict__ u,
-    const float* __restrict__ xz, int di, float* __restrict__ hs, __nv_bfloat16* __restrict__ yhl, long long plane,
+    const float* __restrict__ negA, const float* __restrict__ Dv, const float* __restrict__ xz, int di,
+    float* __restrict__ hs, const __nv_bfloat16* __restrict__ uhl, __nv_bfloat16* __restrict__ yhl, long long plane,
     int T, int W) {
   extern __shared__ float sdelta[];  // [T][ld]
   const int b = blockIdx.x;  // chunks on x (y stops at 65535)
@@ -312,14 +317,19 @@ __global__ void __launch_bounds__(128, CPT == 1 ? 5 : 3) scan_tile_kernel(
   // thread keeps several loads in flight instead of waiting once per position.
   constexpr int PB = CPT == 1 ? 4 : 2;
   const size_t row0 = (size_t)b * T;
-  float cu[CPT][PB], cz[CPT][PB], nu[CPT][PB], nz[CPT][PB];
+  // u is prefetched as its raw hi / lo planes and combined only where it is
+  // used, so the loads stay in flight across a batch
+  __nv_bfloat16 cuh[CPT][PB], cul[CPT][PB], nuh[CPT][PB], nul[CPT][PB];
+  float cz[CPT][PB], nz[CPT][PB];
+  const __nv_bfloat16 bz = __float2bfloat16_rn(0.f);
 #pragma unroll
   for (int j = 0; j < CPT; ++j)
 #pragma unroll
     for (int i = 0; i < PB; ++i) {
       const bool ok = i < T;
       const int c = cbase + 128 * j;
-      cu[j][i] = ok ? u[(row0 + i) * di + c] : 0.f;
+      cuh[j][i] = ok ? uhl[(row0 + i) * di + c] : bz;
+      cul[j][i] = ok ? uhl[plane + (row0 + i) * di + c] : bz;
       cz[j][i] = ok ? xz[(row0 + i) * 2 * di + di + c] : 0.f;
     }
   for (int t0 = 0; t0 < T; t0 += PB) {
@@ -329,7 +339,8 @@ __global__ void __launch_bounds__(128, CPT == 1 ? 5 : 3) scan_tile_kernel(
       for (int i = 0; i < PB; ++i) {
         const bool ok = t0 + PB + i < T;
         const int c = cbase + 128 * j;
-        nu[j][i] = ok ? u[(row0 + t0 + PB + i) * di + c] : 0.f;
+        nuh[j][i] = ok ? uhl[(row0 + t0 + PB + i) * di + c] : bz;
+        nul[j][i] = ok ? uhl[plane + (row0 + t0 + PB + i) * di + c] : bz;
         nz[j][i] = ok ? xz[(row0 + t0 + PB + i) * 2 * di + di + c] : 0.f;
       }
 #pragma unroll
@@ -340,7 +351,8 @@ __global__ void __launch_bounds__(128, CPT == 1 ? 5 : 3) scan_tile_kernel(
         const float4* dl = reinterpret_cast<const float4*>(sdelta + tau * ld);
         float o[CPT];
 #pragma unroll
-        for (int j = 0; j < CPT; ++j) o[j] = scan_update<R>(dl, wdt[j], bdt[j], na[j], h[j], cu[j][i], cz[j][i], dsk[j]);
+        for (int j = 0; j < CPT; ++j)
+          o[j] = scan_update<R>(dl, wdt[j], bdt[j], na[j], h[j], u_from_planes(cuh[j][i], cul[j][i]), cz[j][i], dsk[j]);
 #pragma unroll
         for (int j = 0; j < CPT; ++j) {
           const int c = cbase + 128 * j;
@@ -354,7 +366,7 @@ __global__ void __launch_bounds__(128, CPT == 1 ? 5 : 3) scan_tile_kernel(
 #pragma unroll
     for (int j = 0; j < CPT; ++j)
 #pragma unroll
-      for (int i = 0; i < PB; ++i) { cu[j][i] = nu[j][i]; cz[j][i] = nz[j][i]; }
+      for (int i = 0; i < PB; ++i) { cuh[j][i] = nuh[j][i]; cul[j][i] = nul[j][i]; cz[j][i] = nz[j][i]; }
   }
 #pragma unroll
   for (int j = 0; j < CPT; ++j)
@@ -373,8 +385,9 @@ template <int R>
 __global__ void __launch_bounds__(512) scan_step_kernel(const float* __restrict__ delta, int ld,
                                                         const float* __restrict__ dtw, const float* __restrict__ dtb,
                                                         const float* __restrict__ negA, const float* __restrict__ Dv,
-                                                        const float* __restrict__ u, const float* __restrict__ xz,
+                                                        const float* __restrict__ xz,
                                                         int di, float* __restrict__ hs,
+                                                        const __nv_bfloat16* __restrict__ uhl,
                                                         __nv_bfloat16* __restrict__ yhl, long long plane, int B) {
   // State layout: see scan_state_offset (one contiguous 16 x W block per item).
   // Work item w = (chunk w / n_sl, channel slice w % n_sl); the block's W
@@ -403,7 +416,9 @@ __global__ void __launch_bounds__(512) scan_step_kernel(const float* __restrict_
     uint8_t* p = sm + s * stage_bytes;
     mbar_arrive_expect_tx(&full[s], st_bytes + 2 * uz_bytes + (uint32_t)ld * 4);
     bulk_load(p, state_ptr(w), st_bytes, &full[s]);
-    bulk_load(p + st_bytes, u + (size_t)b * di + c0, uz_bytes, &full[s]);
+    // u as its hi and lo planes
+    bulk_load(p + st_bytes, uhl + (size_t)b * di + c0, uz_bytes / 2, &full[s]);
+    bulk_load(p + st_bytes + uz_bytes / 2, uhl + plane + (size_t)b * di + c0, uz_bytes / 2, &full[s]);
     bulk_load(p + st_bytes + uz_bytes, xz + (size_t)b * 2 * di + di + c0, uz_bytes, &full[s]);
     bulk_load(p + st_bytes + 2 * uz_bytes, delta + (size_t)b * ld, (uint32_t)ld * 4, &full[s]);
   };
@@ -433,13 +448,13 @@ __global__ void __launch_bounds__(512) scan_step_kernel(const float* __restrict_
     if (!mbar_wait(&full[s], (i / kScanStages) & 1)) alive = false;
     if (alive) {
       float* hsm = reinterpret_cast<float*>(p);
-      const float* usm = reinterpret_cast<const float*>(p + st_bytes);
-      const float* zsm = usm + W;
+      const __nv_bfloat16* uhs = reinterpret_cast<const __nv_bfloat16*>(p + st_bytes);  // hi [W] | lo [W]
+      const float* zsm = reinterpret_cast<const float*>(p + st_bytes + uz_bytes);
       const float4* dl = reinterpret_cast<const float4*>(p + st_bytes + 2 * uz_bytes);
       float2 h[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) h[q] = make_float2(hsm[(2 * q) * W + tid], hsm[(2 * q + 1) * W + tid]);
-      const float o = scan_update<R>(dl, wdt, bdt, na, h, usm[tid], zsm[tid], dsk);
+      const float o = scan_update<R>(dl, wdt, bdt, na, h, u_from_planes(uhs[tid], uhs[W + tid]), zsm[tid], dsk);
 #pragma unroll
       for (int q = 0; q < 8; ++q) { hsm[(2 * q) * W + tid] = h[q].x; hsm[(2 * q + 1) * W + tid] = h[q].y; }
       const long long b = w / n_sl;
@@ -466,7 +481,8 @@ __global__ void __launch_bounds__(512) scan_step_kernel(const float* __restrict_
 }
 
 cudaError_t launch_scan(const float* delta, int ld, int r, const float* dtw, const float* dtb, const float* negA,
-                        const float* Dv, const float* u, const float* xz, int di, float* hs, __nv_bfloat16* yhl,
+                        const float* Dv, const float* xz, int di, float* hs, const __nv_bfloat16* uhl,
+                        __nv_bfloat16* yhl,
                         long long plane, int B, int T, cudaStream_t st) {
   if (T == 1 && di <= 1024 && (ld * 4) % 16 == 0) {
     // channel slices of at most 256 (a divisor of di): several small
@@ -483,7 +499,7 @@ cudaError_t launch_scan(const float* delta, int ld, int r, const float* dtw, con
     switch (r) {
 #define BOA_STEP_CASE(RR)                                                                                          \
   case RR:                                                                                                         \
-    scan_step_kernel<RR><<<grid, W, sm, st>>>(delta, ld, dtw, dtb, negA, Dv, u, xz, di, hs, yhl, plane, B);        \
+    scan_step_kernel<RR><<<grid, W, sm, st>>>(delta, ld, dtw, dtb, negA, Dv, xz, di, hs, uhl, yhl, plane, B);        \
     break;
       BOA_STEP_CASE(4)
       BOA_STEP_CASE(8)
@@ -503,9 +519,9 @@ cudaError_t launch_scan(const float* delta, int ld, int r, const float* dtw, con
 #define BOA_SCAN_CASE(RR)                                                                                                \
   case RR:                                                                                                               \
     if (cpt == 2)                                                                                                      \
-      scan_tile_kernel<RR, 2><<<grid, block, sm, st>>>(delta, ld, dtw, dtb, negA, Dv, u, xz, di, hs, yhl, plane, T, W); \
+      scan_tile_kernel<RR, 2><<<grid, block, sm, st>>>(delta, ld, dtw, dtb, negA, Dv, xz, di, hs, uhl, yhl, plane, T, W); \
     else                                                                                                               \
-      scan_tile_kernel<RR, 1><<<grid, block, sm, st>>>(delta, ld, dtw, dtb, negA, Dv, u, xz, di, hs, yhl, plane, T, W); \
+      scan_tile_kernel<RR, 1><<<grid, block, sm, st>>>(delta, ld, dtw, dtb, negA, Dv, xz, di, hs, uhl, yhl, plane, T, W); \
     break;
     BOA_SCAN_CASE(4)
     BOA_SCAN_CASE(8)

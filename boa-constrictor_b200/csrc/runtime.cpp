@@ -357,6 +357,9 @@ int forward(boa_model* m, const boa::TokenSrc& src, int B, int T, int head_mode,
   cudaStream_t st = m->own;
   bf16* hhl = reinterpret_cast<bf16*>(m->xz);   // FF hidden aliases xz (dead after the scan)
   bf16* headh = reinterpret_cast<bf16*>(m->u);  // head hidden aliases u
+  // the scan's y (bf16 hi / lo, plane u_plane) lives in u's fp32 buffer (rows
+  // x di x 4 bytes = two bf16 planes): the Mamba conv writes u only as planes
+  bf16* ybuf = reinterpret_cast<bf16*>(m->u);
   const long long head_plane = (long long)m->rows_cap * d;
   BOA_LAUNCH(PC_EMBED, boa::launch_embed_ln(src, m->emb, d, m->x, m->xn, xn_plane, m->layers[0].ln1w, m->layers[0].ln1b, M, st));
   for (int l = 0; l < m->L; ++l) {
@@ -369,17 +372,17 @@ int forward(boa_model* m, const boa::TokenSrc& src, int B, int T, int head_mode,
       float* sst = m->ssm_st + (size_t)l * m->chunks_cap * 16 * di;
       a.N = 2 * di; a.K = d; a.bias = w.in_b; a.out_f32 = m->xz; a.ld_f32 = 2 * di;
       BOA_LAUNCH(PC_IN_PROJ, boa::gemm_launch(boa::EPI_F32, m->xn, xn_plane, 0, w.in.p, w.in.plane, a, st));
-      BOA_LAUNCH(PC_CONV, boa::launch_conv(m->xz, di, cst, w.conv_w, w.conv_b, m->u, m->uhl, u_plane, B, T, src.pos0,
+      BOA_LAUNCH(PC_CONV, boa::launch_conv(m->xz, di, cst, w.conv_w, w.conv_b, m->uhl, u_plane, B, T, src.pos0,
                                            src.d_pos, st));
       a = boa::GemmArgs{}; a.M = M;
       a.N = m->xpN; a.K = di; a.out_f32 = m->delta; a.ld_f32 = m->xpN;
       BOA_LAUNCH(PC_X_PROJ, boa::gemm_launch(boa::EPI_F32, m->uhl, u_plane, 0, w.xp.p, w.xp.plane, a, st));
-      BOA_LAUNCH(PC_SCAN, boa::launch_scan(m->delta, m->xpN, m->r, w.dt_w, w.dt_b, w.negA, w.Dv, m->u, m->xz, di, sst, m->uhl,
+      BOA_LAUNCH(PC_SCAN, boa::launch_scan(m->delta, m->xpN, m->r, w.dt_w, w.dt_b, w.negA, w.Dv, m->xz, di, sst, m->uhl, ybuf,
                               u_plane, B, T, st));
       a = boa::GemmArgs{}; a.M = M;
       a.N = d; a.K = di; a.bias = w.out_b; a.out_hl = m->xn; a.ld_hl = d; a.plane_hl = xn_plane;
       a.ln_w = w.ln2w; a.ln_b = w.ln2b;
-      BOA_LAUNCH(PC_OUT_PROJ_LN, boa::gemm_launch(boa::EPI_LN_SPLIT, m->uhl, u_plane, 0, w.out.p, w.out.plane, a, st));
+      BOA_LAUNCH(PC_OUT_PROJ_LN, boa::gemm_launch(boa::EPI_LN_SPLIT, ybuf, u_plane, 0, w.out.p, w.out.plane, a, st));
     } else if (m->is_rnn()) {
       // ih for all M rows, then per position: hh (one row per chunk) and the gate update
       const int G = m->gates();
