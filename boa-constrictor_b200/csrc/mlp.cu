@@ -333,27 +333,21 @@ static cudaError_t mlp_launch_t(const CUtensorMap& ta, const CUtensorMap& t1, co
   return cudaGetLastError();
 }
 
-// K-block width of the fused feed-forward.  64 (two 64 KB stages, 128-byte
-// rows) against 32 (four 32 KB stages, 64-byte rows), d_model 256, 16384
-// chunks, alternating runs: 77.2 against 83.5 us per decode launch and 3.71
-// against 3.86 ms per 64-position compress tile, bit-identical.
-static int mlp_bk() { return 64; }
-
-template <int BK>
-static cudaError_t mlp_attrs() {
-  cudaError_t e;
-  if ((e = cudaFuncSetAttribute(mlp_kernel<64, BK>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMlpSmem)) !=
-      cudaSuccess)
-    return e;
-  if ((e = cudaFuncSetAttribute(mlp_kernel<128, BK>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMlpSmem)) !=
-      cudaSuccess)
-    return e;
-  return cudaFuncSetAttribute(mlp_kernel<256, BK>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMlpSmem);
-}
+// K-block width of the fused feed-forward: 64 (two 64 KB stages, 128-byte
+// rows).  Against 32 (four 32 KB stages, 64-byte rows) at d_model 256 with
+// 16384 chunks, alternating runs: 77.2 against 83.5 us per decode launch and
+// 3.71 against 3.86 ms per 64-position compress tile, bit-identical.
+constexpr int kMlpBKUsed = 64;
 
 cudaError_t mlp_prepare_device() {
-  cudaError_t e = mlp_attrs<32>();
-  return e != cudaSuccess ? e : mlp_attrs<64>();
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(mlp_kernel<64, kMlpBKUsed>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kMlpSmem)) != cudaSuccess)
+    return e;
+  if ((e = cudaFuncSetAttribute(mlp_kernel<128, kMlpBKUsed>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kMlpSmem)) != cudaSuccess)
+    return e;
+  return cudaFuncSetAttribute(mlp_kernel<256, kMlpBKUsed>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMlpSmem);
 }
 
 cudaError_t mlp_launch(const __nv_bfloat16* xn, long long xn_plane, const __nv_bfloat16* w1, long long w1_plane,
@@ -362,22 +356,14 @@ cudaError_t mlp_launch(const __nv_bfloat16* xn, long long xn_plane, const __nv_b
   const int D = a.N;
   if (a.M <= 0 || !a.res || !a.out_hl || !a.bias || !b1 || (D != 64 && D != 128 && D != 256))
     return cudaErrorInvalidValue;
-  const int bk = mlp_bk();
   CUtensorMap ta, t1, t2;
-  if (!make_plane_map(&ta, xn, D, a.M, xn_plane, kBM, bk)) return cudaErrorInvalidValue;
-  if (!make_plane_map(&t1, w1, D, 4 * D, w1_plane, kMlpHC, bk)) return cudaErrorInvalidValue;
-  if (!make_plane_map(&t2, w2, 4 * D, D, w2_plane, D, bk)) return cudaErrorInvalidValue;
-  if (bk == 64) {
-    switch (D) {
-      case 64: return mlp_launch_t<64, 64>(ta, t1, t2, b1, a, stream);
-      case 128: return mlp_launch_t<128, 64>(ta, t1, t2, b1, a, stream);
-      default: return mlp_launch_t<256, 64>(ta, t1, t2, b1, a, stream);
-    }
-  }
+  if (!make_plane_map(&ta, xn, D, a.M, xn_plane, kBM, kMlpBKUsed)) return cudaErrorInvalidValue;
+  if (!make_plane_map(&t1, w1, D, 4 * D, w1_plane, kMlpHC, kMlpBKUsed)) return cudaErrorInvalidValue;
+  if (!make_plane_map(&t2, w2, 4 * D, D, w2_plane, D, kMlpBKUsed)) return cudaErrorInvalidValue;
   switch (D) {
-    case 64: return mlp_launch_t<64, 32>(ta, t1, t2, b1, a, stream);
-    case 128: return mlp_launch_t<128, 32>(ta, t1, t2, b1, a, stream);
-    default: return mlp_launch_t<256, 32>(ta, t1, t2, b1, a, stream);
+    case 64: return mlp_launch_t<64, kMlpBKUsed>(ta, t1, t2, b1, a, stream);
+    case 128: return mlp_launch_t<128, kMlpBKUsed>(ta, t1, t2, b1, a, stream);
+    default: return mlp_launch_t<256, kMlpBKUsed>(ta, t1, t2, b1, a, stream);
   }
 }
 
